@@ -8,14 +8,20 @@ configs -- sum and mean of x: f32[2^26] ~ U(-1, 1) -- each compiled from its
 Kernel IR by ``compile.py``'s pipeline and launched through ``libemmyrt``.
 Inputs (256 MiB) are larger than the 126 MB L2, so no flush is needed.
 With N GPUs (torchrun, one process per GPU) every rank reduces its own 2^26
-shard and one NCCL all-reduce of the two scalars finishes the global sum and
-mean (weak scaling).
+shard and the library's fold kernel (emmy_rt_fold_f32: peer stores over NVLink)
+sums the two scalars over the ranks, giving the global sum and mean (weak
+scaling); ``--collective nccl`` uses an NCCL all-reduce instead.
 
 Printed JSON: ``value`` = algorithmic GB/s of the whole job (device-resident
-inputs, CUDA events, max over ranks); ``e2e`` = the same through the C ABI
-``emmy_rt_run`` with host buffers (H2D + launch + D2H in the timed region);
-``roofline`` for the dominant kernel against the measured HBM copy
-bandwidth; ``cpu_baseline`` = PyTorch CPU of the same expressions.
+inputs, CUDA events, max over ranks); ``e2e`` = the same through the C ABI with
+host buffers (H2D + launches + D2H in the timed region); ``roofline`` for the
+dominant kernel against the measured HBM copy bandwidth; ``cpu_baseline`` =
+PyTorch CPU of the same expressions. At N = 1 ``per_config`` adds one entry per
+benchmark configuration (pointwise add, sum, mean, RMSNorm, softmax, L2-norm,
+both matmuls, both attentions): CUDA-event median per launch with L2 flushed
+(or a working set above twice L2), fraction of the roofline, compile ms, the
+kernel's error word, its largest error against an fp64 result of the same
+inputs, and PyTorch CPU of the same expression.
 """
 
 from __future__ import annotations
@@ -42,6 +48,8 @@ PER_KERNEL = 10               # steps of the per-kernel (event-bracketed) timing
 HBM_NOMINAL_GBS = 8000.0      # B200 HBM3e nominal bandwidth, for context beside the measured peak
 RES_SLOTS = 4                 # result slots: an all-reduce may lag its step by 3 steps
 FALLBACK_HBM_GBS = 6650.0
+REF_STEP_S = 0.15             # reference arm: seconds of CPU work per step
+E2E_STEPS = 30                # e2e: timed steps (median)
 
 
 def measured_peaks():
@@ -165,6 +173,10 @@ def compile_process_ms(make, repeats=5):
 # ---------------------------------------------------------------------------
 
 def run_reference(args, rank, world):
+    """The reference arm: PyTorch CPU of the same expressions (x.sum(), x.mean()) on all host
+    cores, on rank 0 only. A step is a bounded sample of the workload: back-to-back passes
+    over the full x for about REF_STEP_S seconds (the same measurement as ``cpu_baseline``,
+    split into ``--steps`` parts), after ``--warmup`` untimed steps."""
     if rank != 0:
         return 0
     from oracle import cpu_baseline as cb
@@ -172,13 +184,13 @@ def run_reference(args, rank, world):
     x = cb.reduce_inputs(N_REDUCE)
     bytes_step = 2 * (4 * N_REDUCE) + 4 + 4 + 4
     for _ in range(max(args.warmup, 1)):
-        cb.reduce_step(x)
-    times = []
+        cb.reduce_rate(x, REF_STEP_S)
+    per_step, passes = [], 0
     for _ in range(args.steps):
-        t0 = time.perf_counter()
-        cb.reduce_step(x)
-        times.append(time.perf_counter() - t0)
-    sec = sum(times) / len(times)
+        sec, n = cb.reduce_rate(x, REF_STEP_S)
+        per_step.append(sec)
+        passes += n
+    sec = statistics.mean(per_step)
     gbs = bytes_step / sec / 1e9
     line = {
         "metric": METRIC, "impl": "reference", "value": round(gbs, 3), "unit": "GB/s",
@@ -187,8 +199,8 @@ def run_reference(args, rank, world):
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": _config(world),
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
-                         "sample": f"torch CPU x.sum() and x.mean(), x f32[2^26], "
-                                   f"{args.steps} steps"},
+                         "sample": f"torch CPU x.sum() and x.mean() of the full x f32[2^26]: "
+                                   f"{args.steps} steps of ~{REF_STEP_S} s, {passes} passes"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -216,15 +228,8 @@ def cpu_baseline_leg():
     cores = cb.threads()
     x = cb.reduce_inputs(N_REDUCE)
     bytes_step = 2 * (4 * N_REDUCE) + 12
-    t_end = time.perf_counter() + 3.0
-    n, t = 0, 0.0
-    cb.reduce_step(x)
-    while time.perf_counter() < t_end or n < 3:
-        t0 = time.perf_counter()
-        cb.reduce_step(x)
-        t += time.perf_counter() - t0
-        n += 1
-    return {"value": round(bytes_step / (t / n) / 1e9, 3), "unit": "GB/s", "cores": cores,
+    sec, n = cb.reduce_rate(x, 3.0)
+    return {"value": round(bytes_step / sec / 1e9, 3), "unit": "GB/s", "cores": cores,
             "kind": "port",
             "sample": f"torch CPU x.sum() and x.mean() of the full x f32[2^26], {n} steps "
                       f"(~3 s)"}
@@ -316,6 +321,8 @@ def run_ours(args, rank, world, local_rank):
                 pending[slot] = dist.all_reduce(res[slot], async_op=True)
 
     # correctness of this run's result against the fp64 sum of the device data
+    if world > 1:
+        dist.barrier()          # the first fold: every rank's mailbox is mapped by now
     step(0)
     drain()
     torch.cuda.synchronize()
@@ -394,6 +401,12 @@ def run_ours(args, rank, world, local_rank):
     # e2e through the C ABI with host buffers (H2D + launch + D2H timed per step)
     e2e = _e2e(runtime, ptx_s, k_s, ptx_m, k_m, local_rank, world, dev, fold)
     fold_err = fold.error_word() if fold is not None else 0      # every fold of this run
+    if world > 1:
+        # a fold whose wait ran out returns at once from then on: the timed steps of that
+        # rank then exchanged nothing, so the run has no valid number on any rank
+        fe = torch.tensor([float(fold_err)], device=dev, dtype=torch.float64)
+        dist.all_reduce(fe, op=dist.ReduceOp.MAX)
+        fold_err = int(fe.item())
 
     result = {
         "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
@@ -433,7 +446,12 @@ def run_ours(args, rank, world, local_rank):
         "e2e": e2e,
         "clocks": clocks.summary(t0, t1),
     }
+    if fold_err:
+        result["value"] = None
+        result["invalid"] = (f"emmy_rt_fold_f32 error word {fold_err:#x}: a fold's bounded wait "
+                             "ran out, so later steps exchanged nothing between ranks")
     if rank == 0 and world == 1:
+        result["per_config"] = per_config(args, peaks, local_rank)
         result["cpu_baseline"] = cpu_baseline_leg()
     if rank == 0:
         print(json.dumps(result), flush=True)
@@ -441,7 +459,7 @@ def run_ours(args, rank, world, local_rank):
     mod_m.close()
     if fold is not None:
         fold.close()
-    return 0
+    return 1 if fold_err else 0
 
 
 def _e2e(runtime, ptx_s, k_s, ptx_m, k_m, local_rank, world, dev, fold=None):
@@ -488,7 +506,7 @@ def _e2e(runtime, ptx_s, k_s, ptx_m, k_m, local_rank, world, dev, fold=None):
         for _ in range(2):
             step()
         times = []
-        for _ in range(5):
+        for _ in range(E2E_STEPS):
             t0 = time.perf_counter()
             step()
             times.append((time.perf_counter() - t0) * 1e6)
@@ -527,100 +545,197 @@ def _e2e(runtime, ptx_s, k_s, ptx_m, k_m, local_rank, world, dev, fold=None):
 
 
 # ---------------------------------------------------------------------------
-# suite: one line per workload (device-resident, L2 flushed between launches)
+# per configuration: every benchmark workload once (device-resident, L2 flushed)
 # ---------------------------------------------------------------------------
 
-def measured_tf32_tflops():
-    """cuBLAS TF32 GEMM throughput on this GPU (8192^3, best of 10): the TF32 tensor peak."""
+TENSOR_DENOM = "bf16_tflops / 2 / 3"   # dense TF32 is half the bf16 rate; 3xTF32 = 3 products
+
+
+def tf32x3_ceiling(peaks):
+    """The contraction roofline: the measured dense bf16 GEMM rate / 2 (TF32) / 3 (3xTF32)."""
+    return peaks["bf16_tflops"] / 2.0 / 3.0
+
+
+def _algorithmic(name, k):
+    """(work per launch, unit, bound) of a benchmark workload from its argument shapes."""
+    import numpy as np
+    shp = {a["name"]: a["shape"] for a in k["args"]}
+    if name.startswith("matmul"):
+        (M, K_), (_, N) = shp["x0"], shp["x1"]
+        return 2.0 * M * N * K_, "FLOP", "tensor"
+    if name.startswith("attention"):
+        Bq, Hq, Sq, D = shp["q"]
+        return 4.0 * Bq * Hq * Sq * shp["kt"][-1] * D, "FLOP", "tensor"
+    return float(sum(4 * int(np.prod(a.get("shape") or [1])) for a in k["args"])), "B", "hbm"
+
+
+def fp64_error(name, inputs, got, device):
+    """Largest error of ``got`` against the fp64 result of the same inputs, computed on the GPU
+    in float64 with torch (a checker beside the measurement, not part of the timed path).
+
+    Row normalisations and sums: the largest element-wise relative error |got - ref| / |ref|
+    (bound 1e-5). Contractions: the largest |got - ref| / (|ref| + row max|ref|) (bound 1e-4).
+    Pointwise add: the number of elements that differ from the f32 sum (bound 0)."""
+    import numpy as np
     import torch
-    torch.backends.cuda.matmul.allow_tf32 = True
-    a = torch.randn(8192, 8192, device="cuda")
-    b = torch.randn(8192, 8192, device="cuda")
-    for _ in range(3):
-        a @ b
-    best = 0.0
-    for _ in range(10):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        a @ b
-        e1.record()
-        torch.cuda.synchronize()
-        best = max(best, 2 * 8192 ** 3 / (e0.elapsed_time(e1) * 1e-3) / 1e12)
-    torch.backends.cuda.matmul.allow_tf32 = False
-    del a, b
-    return best
+
+    def t64(a):
+        return torch.from_numpy(np.ascontiguousarray(a)).to(device, torch.float64)
+    g = t64(got)
+    if name == "add":
+        want = torch.from_numpy(inputs["x0"] + inputs["x1"]).to(device)
+        diff = int((torch.from_numpy(got).to(device) != want).sum().item())
+        return {"form": "elements differing from f32 x0 + x1", "value": diff, "bound": 0,
+                "ok": diff == 0}
+    if name in ("sum", "mean", "rmsnorm", "softmax", "l2norm"):
+        x = t64(inputs["x"])
+        if name == "sum":
+            ref = x.sum().reshape(1)
+        elif name == "mean":
+            ref = x.mean().reshape(1)
+        elif name == "rmsnorm":
+            ref = x * torch.rsqrt((x * x).mean(-1, keepdim=True) + 1e-6) * t64(inputs["w"])
+        elif name == "softmax":
+            ref = torch.softmax(x, -1)
+        else:
+            ref = x / torch.clamp(x.norm(dim=-1, keepdim=True), min=1e-12)
+        g = g.reshape(ref.shape)
+        err = float(((g - ref).abs() / ref.abs()).max().item())
+        return {"form": "max |got - ref| / |ref| (element-wise)", "value": float(f"{err:.3e}"),
+                "bound": 1e-5, "ok": err <= 1e-5}
+    if name.startswith("matmul"):
+        ref = t64(inputs["x0"]) @ t64(inputs["x1"])
+        refs = [(g.reshape(ref.shape), ref)]
+    else:
+        c = float(inputs["div_c1"].reshape(-1)[0])
+        q, kt, v = inputs["q"], inputs["kt"], inputs["v"]
+        g = g.reshape(q.shape)
+        refs = []
+        for b in range(q.shape[0]):       # one batch entry (all heads) at a time
+            s_ = torch.softmax((t64(q[b]) @ t64(kt[b])) / c, -1)
+            refs.append((g[b], s_ @ t64(v[b])))
+    err = 0.0
+    for gb, rb in refs:
+        rowmax = rb.abs().amax(-1, keepdim=True)
+        err = max(err, float(((gb - rb).abs() / (rb.abs() + rowmax)).max().item()))
+    return {"form": "max |got - ref| / (|ref| + row max|ref|)", "value": float(f"{err:.3e}"),
+            "bound": 1e-4, "ok": err <= 1e-4}
 
 
-def run_suite(args):
+def measure_config(name, args, peaks, l2, flush, *, device=0, compile_repeats=5,
+                   process_repeats=3, cpu=True, check=True):
+    """One benchmark workload: compile it (in-process median and ``python compile.py``
+    process time), run it once on the seeded inputs for the fp64 check, then time ``steps``
+    launches with CUDA events (L2 flushed by a 256 MiB memset before each launch unless the
+    working set is above twice L2, in which case it streams from HBM anyway)."""
     import numpy as np
     from emmyptx import runtime, workloads
     from emmyptx.inputs import kernel_inputs
+    ptx, template, meta, k, cms = compile_workload(workloads.WORKLOADS[name],
+                                                   repeats=compile_repeats)
+    proc_ms = compile_process_ms(workloads.WORKLOADS[name], repeats=process_repeats) \
+        if process_repeats else None
+    mod = runtime.Module(ptx, k["entry"], device)
+    inputs = kernel_inputs(k)
+    bufs, outs, footprint = [], {}, 0
+    for a in k["args"]:
+        shape = tuple(a.get("shape") or (1,))
+        nbytes = 4 * int(np.prod(shape))
+        footprint += nbytes
+        if a.get("output"):
+            b = runtime.DeviceBuffer(nbytes)
+            b.zero()
+            outs[a["name"]] = (b, shape)
+        else:
+            b = runtime.DeviceBuffer.from_array(inputs[a["name"]])
+        bufs.append(b)
+    ptrs = [b.ptr for b in bufs]
+    work, unit, bound = _algorithmic(name, k)
+    entry = {"entry": k["entry"], "template": template, "grid": k["grid"][0],
+             "block": k["block"][0], "smem_bytes": k.get("smem_bytes", 0),
+             "registers": mod.attrs()["registers"]}
+    try:
+        if check:
+            mod.launch(k["grid"], k["block"], k.get("smem_bytes", 0), ptrs)
+            runtime.sync()
+            (b, shape), = outs.values()
+            got = b.download(np.zeros(shape, np.float32))
+            entry["fp64_check"] = fp64_error(name, inputs, got, f"cuda:{device}")
+        do_flush = footprint < 2 * l2
+        ms = mod.time(k["grid"], k["block"], k.get("smem_bytes", 0), ptrs,
+                      iters=args.steps, warmup=args.warmup,
+                      flush_ptr=flush.ptr if do_flush else 0,
+                      flush_bytes=flush.nbytes if do_flush else 0)
+        entry["error_word"] = mod.error_word()
+    finally:
+        mod.close()
+        for b in bufs:
+            b.free()
+    us = statistics.median(ms) * 1e3
+    entry.update({"us_median": round(us, 3), "us_min": round(min(ms) * 1e3, 3),
+                  "launches": args.steps, "l2_flush": do_flush,
+                  "compile_ms": round(cms, 2)})
+    if proc_ms is not None:
+        entry["compile_process_ms"] = round(proc_ms, 1)
+    if bound == "hbm":
+        gbs = work / (us * 1e-6) / 1e9
+        entry["roofline"] = {"bound": "hbm", "algorithmic_bytes": int(work),
+                             "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
+                             "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
+                             "peak_source": f"{peaks['source']} hbm_gbs (burst copy)"}
+    else:
+        tfl = work / (us * 1e-6) / 1e12
+        ceil = tf32x3_ceiling(peaks)
+        entry["roofline"] = {"bound": "tensor", "algorithmic_flops": work,
+                             "achieved": round(tfl, 2), "peak": round(ceil, 1),
+                             "unit": "TFLOP/s", "frac": round(tfl / ceil, 4),
+                             "peak_source": f"{peaks['source']} {TENSOR_DENOM}"}
+    if cpu:
+        from oracle import cpu_baseline as cb
+        entry["cpu_baseline"] = cb.workload_baseline(
+            name, inputs, algorithmic=work, unit="GB/s" if bound == "hbm" else "TFLOP/s")
+    return entry
+
+
+def per_config(args, peaks, device=0):
+    """Every benchmark configuration once on this GPU (``measure_config``)."""
+    from emmyptx import runtime, workloads
+    l2 = runtime.device_info(device)["l2_bytes"]
+    flush = runtime.DeviceBuffer(256 << 20)
+    out = {}
+    try:
+        for name in workloads.WORKLOADS:
+            out[name] = measure_config(name, args, peaks, l2, flush, device=device)
+    finally:
+        flush.free()
+    return out
+
+
+# ---------------------------------------------------------------------------
+# suite: one line per workload (device-resident, L2 flushed between launches)
+# ---------------------------------------------------------------------------
+
+def run_suite(args):
+    """One line per workload: ``measure_config`` (timing, roofline, compile ms, fp64 check,
+    CPU baseline), plus the fixed cost of an empty kernel under the same launch for the
+    memory-bound ones and the reference compiler's PTX of the same computation."""
+    from emmyptx import runtime, workloads
     runtime.init(0)
     ref_variants = _reference_ptx_variants()
     peaks = measured_peaks()
     l2 = runtime.device_info(0)["l2_bytes"]
     flush = runtime.DeviceBuffer(256 << 20)
     names = args.only.split(",") if args.only else list(workloads.WORKLOADS)
-    tf32 = None
     for name in names:
-        ptx, template, meta, k, cms = compile_workload(workloads.WORKLOADS[name], repeats=20)
-        proc_ms = compile_process_ms(workloads.WORKLOADS[name])
-        mod = runtime.Module(ptx, k["entry"])
-        inputs = kernel_inputs(k)
-        bufs, alg = [], 0
-        for a in k["args"]:
-            shape = tuple(a.get("shape") or (1,))
-            nbytes = 4 * int(np.prod(shape))
-            alg += nbytes
-            if a.get("output"):
-                b = runtime.DeviceBuffer(nbytes)
-                b.zero()
-            else:
-                b = runtime.DeviceBuffer.from_array(inputs[a["name"]])
-            bufs.append(b)
-        # inputs+outputs larger than twice L2 stream from HBM anyway; smaller ones get a flush
-        do_flush = alg < 2 * l2
-        ms = mod.time(k["grid"], k["block"], k.get("smem_bytes", 0), [b.ptr for b in bufs],
-                      iters=args.steps, warmup=args.warmup, flush_ptr=flush.ptr if do_flush else 0,
-                      flush_bytes=flush.nbytes if do_flush else 0)
-        us = statistics.median(ms) * 1e3
-        line = {"workload": name, "entry": k["entry"], "template": template,
-                "us_median": round(us, 3), "compile_ms": round(cms, 2),
-                "compile_process_ms": round(proc_ms, 1),
-                "registers": mod.attrs()["registers"], "l2_flush": do_flush,
-                "grid": k["grid"][0], "block": k["block"][0], "smem_bytes": k.get("smem_bytes", 0)}
-        shp = {a["name"]: a["shape"] for a in k["args"]}
-        if template in ("contraction", "attention"):
-            if template == "contraction":
-                (M, K_), (_, N) = shp["x0"], shp["x1"]
-                flops = 2.0 * M * N * K_
-            else:                         # q @ kt and P @ v: 2 * 2 * S_q * S_kv * D per head
-                Bq, Hq, Sq, D = shp["q"]
-                flops = 4.0 * Bq * Hq * Sq * shp["kt"][-1] * D
-            if tf32 is None:
-                tf32 = measured_tf32_tflops()
-            tfl = flops / (us * 1e-6) / 1e12
-            line.update({"algorithmic_flops": flops, "tflops": round(tfl, 2),
-                         "tf32_peak_tflops_measured": round(tf32, 1),
-                         "frac_of_tf32_over_3": round(tfl / (tf32 / 3), 4)})
-        else:
-            gbs = alg / (us * 1e-6) / 1e9
-            floor = _empty_kernel_us(k, len(bufs), args, flush)
-            line.update({"algorithmic_bytes": alg, "gbs": round(gbs, 1),
-                         "frac_hbm": round(gbs / peaks["hbm_gbs"], 4),
-                         "launch_floor_us": round(floor, 3)})
-        line["error_word"] = mod.error_word()
-        mod.close()
-        for b in bufs:
-            b.free()
-        if not args.no_cpu:
-            from oracle import cpu_baseline as cb
-            work, unit = ((line["algorithmic_flops"], "TFLOP/s") if "algorithmic_flops" in line
-                          else (line["algorithmic_bytes"], "GB/s"))
-            line["cpu_baseline"] = cb.workload_baseline(name, inputs, algorithmic=work,
-                                                        unit=unit)
+        line = {"workload": name}
+        line.update(measure_config(name, args, peaks, l2, flush, compile_repeats=20,
+                                   process_repeats=5, cpu=not args.no_cpu))
+        if line["roofline"]["bound"] == "hbm":
+            k = workloads.WORKLOADS[name]()[1]["kernels"][0]
+            line["launch_floor_us"] = round(_empty_kernel_us(k, len(k["args"]), args, flush), 3)
         if name in ref_variants:
-            line["reference_ptx"] = _time_reference_ptx(ref_variants[name], us, args, flush, l2)
+            line["reference_ptx"] = _time_reference_ptx(ref_variants[name], line["us_median"],
+                                                        args, flush, l2)
         print(json.dumps(line), flush=True)
 
 

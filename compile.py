@@ -17,6 +17,19 @@ if _PKG not in sys.path:
     sys.path.insert(0, _PKG)
 
 
+# The reference's public classes, importable from this module as its tests do
+# (``from compile import EmmyIRParser, EmmyKernelIR, PTXKernelGenerator``); resolved on
+# first use so that the command line path imports nothing extra.
+_API = ("EmmyKernelIR", "EmmyIRParser", "PTXKernelGenerator", "EmmyIRLowering", "PTXEmitter")
+
+
+def __getattr__(name):
+    if name in _API:
+        import emmyptx
+        return getattr(emmyptx, name)
+    raise AttributeError(name)
+
+
 def main(argv=None) -> int:
     argv = sys.argv if argv is None else argv
     if len(argv) != 2:

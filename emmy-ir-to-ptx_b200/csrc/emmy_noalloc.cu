@@ -17,8 +17,17 @@
 //    GPU (different streams, or different host threads) race on it and give
 //    wrong results; serialise them.
 //  * The first call on each device looks up the array's device address with
-//    cudaGetSymbolAddress (with that device current). Make that first call
-//    before any stream capture begins.
+//    cudaGetSymbolAddress (with that device current). Under CUDA's lazy module
+//    loading (the default since CUDA 12.2) that first call is also what loads
+//    this file's device code and its 16,640-byte array onto the device, so make
+//    it before the host's pool reserves the device's memory, and before any
+//    stream capture begins.
+//  * Calls outside stream capture look the address up again (cheap once the
+//    module is loaded), so a reset of the device's primary context (after
+//    cudaDeviceReset, say) is picked up; a call on a capturing stream uses the
+//    address of the last call made outside capture on that device.
+//  * x and out must be 4-byte aligned (they are float arrays); other pointers
+//    are refused before anything is launched.
 
 #include "emmy_rt.h"
 
@@ -109,19 +118,29 @@ int fail(int code, const char *what, cudaError_t e) {
   return code;
 }
 
-// Device address of the scratch array for the current device (looked up once per device).
-int scratch_for_current_device(unsigned int **out) {
+// Device address of the scratch array for the current device. Outside stream capture it is
+// looked up on every call (so a context that was reset and made again is seen); a capturing
+// stream uses the address the last uncaptured call on this device found, since a lookup that
+// has to load the module is not allowed while a capture is running.
+int scratch_for_current_device(cudaStream_t s, unsigned int **out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(EMMY_RT_ECUDA, "cudaGetDevice", e);
   if (dev < 0 || dev >= kMaxDevices) return fail(EMMY_RT_EINVAL, "device index out of range",
                                                   cudaSuccess);
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  e = cudaStreamIsCapturing(s, &cs);
+  if (e != cudaSuccess) return fail(EMMY_RT_ECUDA, "cudaStreamIsCapturing", e);
   std::lock_guard<std::mutex> lock(g_mu);
-  if (!g_scratch_addr[dev]) {
+  if (cs == cudaStreamCaptureStatusNone) {
     void *p = nullptr;
     e = cudaGetSymbolAddress(&p, emmy_noalloc_scratch);
     if (e != cudaSuccess) return fail(EMMY_RT_ECUDA, "cudaGetSymbolAddress", e);
     g_scratch_addr[dev] = static_cast<unsigned int *>(p);
+  } else if (!g_scratch_addr[dev]) {
+    return fail(EMMY_RT_EINVAL,
+                "first call on this device made during stream capture: call once before "
+                "capturing so the scratch address is known", cudaSuccess);
   }
   *out = g_scratch_addr[dev];
   return EMMY_RT_OK;
@@ -132,6 +151,8 @@ int scratch_for_current_device(unsigned int **out) {
 extern "C" int emmy_rt_sum_f32_noalloc(uint64_t x, uint64_t n, uint64_t out, uint32_t grid,
                                        uint64_t stream) {
   if (!x || !out) return fail(EMMY_RT_EINVAL, "null buffer", cudaSuccess);
+  if ((x | out) & 3u)
+    return fail(EMMY_RT_EINVAL, "x and out must be 4-byte aligned (f32 arrays)", cudaSuccess);
   if (grid == 0 || grid > EMMY_RT_NOALLOC_MAX_CTAS) {
     char msg[160];
     snprintf(msg, sizeof(msg), "grid %u outside 1..%d (the fixed scratch holds %d partials)",
@@ -139,10 +160,10 @@ extern "C" int emmy_rt_sum_f32_noalloc(uint64_t x, uint64_t n, uint64_t out, uin
     emmy_rt_internal_set_error(msg);
     return EMMY_RT_EINVAL;
   }
-  unsigned int *scratch = nullptr;
-  int rc = scratch_for_current_device(&scratch);
-  if (rc) return rc;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(static_cast<uintptr_t>(stream));
+  unsigned int *scratch = nullptr;
+  int rc = scratch_for_current_device(s, &scratch);
+  if (rc) return rc;
   // the ticket must start at zero even if an earlier call was cut short
   cudaError_t e = cudaMemsetAsync(scratch + kTicketSlot, 0, sizeof(unsigned int), s);
   if (e != cudaSuccess) return fail(EMMY_RT_ECUDA, "cudaMemsetAsync", e);

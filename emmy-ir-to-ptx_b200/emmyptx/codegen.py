@@ -103,7 +103,7 @@ def identity_literal(op: str) -> str:
 
 
 def run_program(gen, program, env: dict, *, load=None, write=None, accum_regs=None,
-                lets=None):
+                lets=None, accum=None):
     """Emit an element program.
 
     ``env`` maps SSA names to registers and is updated in place. ``load(p)``
@@ -111,6 +111,8 @@ def run_program(gen, program, env: dict, *, load=None, write=None, accum_regs=No
     :class:`ElemWrite`. ``accum_regs`` maps accumulator names to their
     carried registers, updated by :class:`ElemAccum` entries; a program may read
     an accumulator before its ``Accum`` statement (the online-softmax update).
+    ``accum(p, base, value, acc)``, when given, emits the update of accumulator
+    ``acc`` instead of the plain accumulate op (a compensated sum).
     """
     if accum_regs:
         for name, reg in accum_regs.items():
@@ -134,7 +136,10 @@ def run_program(gen, program, env: dict, *, load=None, write=None, accum_regs=No
         elif isinstance(p, ElemAccum):
             acc = accum_regs[p.name]
             base = env[p.base] if p.base is not None else acc
-            emit_op(gen, p.op, [base, env[p.value]], dst=acc)
+            if accum is not None:
+                accum(p, base, env[p.value], acc)
+            else:
+                emit_op(gen, p.op, [base, env[p.value]], dst=acc)
             env[p.name] = acc
         elif isinstance(p, ElemWrite):
             write(p, env[p.value])

@@ -150,11 +150,14 @@ class PTXKernelGenerator:
     # -- body -----------------------------------------------------------
     @staticmethod
     def _validate_line(line: str) -> str:
+        """One instruction per call: a line break anywhere (a trailing one included) is
+        refused before the surrounding blanks are stripped (reference ``compile.py:2096-2119``)."""
         if type(line) is not str:
             raise TypeError("PTX instruction must be text")
+        if "\n" in line or "\r" in line:
+            raise ValueError("Expected exactly one ASCII PTX instruction")
         text = line.strip()
-        if text.count(";") != 1 or text[-1:] != ";" or not text.isascii() or "\n" in text \
-                or "\r" in text:
+        if text.count(";") != 1 or text[-1:] != ";" or not text.isascii():
             raise ValueError("Expected exactly one ASCII PTX instruction")
         return text
 
@@ -177,12 +180,15 @@ class PTXKernelGenerator:
         self._lines.append(f"{name}:")
 
     def thread_index_1d(self) -> str:
-        """``%ctaid.x * %ntid.x + %tid.x`` in a fresh ``.u32`` register."""
-        tid, bid, ntid, index = (self.register(".u32") for _ in range(4))
+        """``%ctaid.x * %ntid.x + %tid.x`` in a fresh ``.u32`` register: the reference's
+        instruction sequence and register numbering (``compile.py:2201-2228``); ptxas fuses
+        the multiply and add."""
+        tid, bid, ntid, prod, index = (self.register(".u32") for _ in range(5))
         self.emit(f"mov.u32 {tid}, %tid.x;")
         self.emit(f"mov.u32 {bid}, %ctaid.x;")
         self.emit(f"mov.u32 {ntid}, %ntid.x;")
-        self.emit(f"mad.lo.u32 {index}, {bid}, {ntid}, {tid};")
+        self.emit(f"mul.lo.u32 {prod}, {bid}, {ntid};")
+        self.emit(f"add.u32 {index}, {prod}, {tid};")
         return index
 
     # -- rendering ------------------------------------------------------

@@ -139,8 +139,9 @@ def contraction_tc(seed: int):
     """A random matmul inside the tcgen05 template's conditions (M % 128, K % 32, 256
     threads, dynamic shared memory), small enough for a quick fp64 check: grids come out even
     and odd, so both the CTA-pair and the single-CTA forms occur, with several tiles per CTA
-    or cluster and, for some, half-width units (compile with ``template="contraction"``:
-    shapes this small would otherwise go to the walker)."""
+    or cluster and, for some, half-width units; some in the split-K form with atomic writes
+    (compile with ``template="contraction"``: shapes this small would otherwise go to the
+    walker)."""
     rng = random.Random(seed)
     TN, RN = rng.choice([(256, 16), (128, 8)])
     M = 128 * rng.randint(1, 8)
@@ -151,8 +152,12 @@ def contraction_tc(seed: int):
         # 128-wide IR tiles with four stages offer the shared memory of 256-wide pair tiles:
         # then the template's tiles are half as many as the clusters, all run as half units
         TN, RN, S, M = 128, 8, 4, 256 * rng.randint(1, 4)
-    payload, meta = workloads.matmul(M, N, K, TM=128, TN=TN, RM=8, RN=RN, S=S)
-    return payload, meta, {"M": M, "N": N, "K": K, "TN": TN, "S": S}
+    # some in the split-K form (atomic writes into a zeroed output, as the m02 fixture)
+    splits = rng.choice([1, 1, 2, 3, 4])
+    if (K // 32) % splits:
+        splits = 1
+    payload, meta = workloads.matmul(M, N, K, TM=128, TN=TN, RM=8, RN=RN, S=S, splits=splits)
+    return payload, meta, {"M": M, "N": N, "K": K, "TN": TN, "S": S, "splits": splits}
 
 
 def attention(seed: int):

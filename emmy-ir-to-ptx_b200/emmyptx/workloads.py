@@ -338,15 +338,28 @@ WORKLOADS = {
 # matmul (m01 structure): per-thread RM x RN FMA tiles fed by an S-stage cp.async ring
 # ---------------------------------------------------------------------------
 
-def matmul(M=4096, N=4096, K=4096, TM=128, TN=256, RM=8, RN=16, BKs=32, S=4, std=None):
-    """C = A @ B with A[M,K], B[K,N] row-major; IR schedule like the m01 fixture."""
+def matmul(M=4096, N=4096, K=4096, TM=128, TN=256, RM=8, RN=16, BKs=32, S=4, std=None,
+           splits=1):
+    """C = A @ B with A[M,K], B[K,N] row-major; IR schedule like the m01 fixture.
+
+    ``splits > 1`` writes the split-K form of the m02 fixture: a leading Tile axis
+    ``_a2_ks`` over the K splits (grid = splits x output tiles), each CTA's K loop covering
+    K / splits from ``_a2_ks * K / splits``, and atomic writes (``red.global.add``) into an
+    output that the runner zeroes before every launch (``zero_outputs``)."""
     tu_m, tu_n = TM // RM, TN // RN
     T = tu_m * tu_n
     assert M % TM == 0 and N % TN == 0 and K % BKs == 0 and (TM * BKs // 4) % T == 0 \
-        and (BKs * TN // 4) % T == 0
+        and (BKs * TN // 4) % T == 0 and splits >= 1 and (K // BKs) % splits == 0
     a0b, a1b, a0u, a1u = (Var(name=n) for n in ("a0_b", "a1_b", "a0_u", "a1_u"))
     lin = _bin("+", _bin("*", a0u, _lit(tu_n)), a1u)
     ks = Var(name="_ks")
+    Kp = K // splits                     # K extent of one split
+
+    def kx(e):
+        """A K index of this CTA's split: the split's offset plus ``e``."""
+        if splits == 1:
+            return e
+        return _bin("+", _bin("*", Var(name="_a2_ks"), _lit(Kp)), e)
 
     def copies(stage_expr, k_expr):
         out = []
@@ -356,14 +369,14 @@ def matmul(M=4096, N=4096, K=4096, TM=128, TN=256, RM=8, RN=16, BKs=32, S=4, std
             out.append(CpAsyncCopy(
                 smem="_a_smem", smem_index=(_bin("+", _bin("*", stage_expr, _lit(TM)), row), col),
                 src="x0", src_index=(_bin("+", _bin("*", a0b, _lit(TM)), row),
-                                     _bin("+", k_expr, col)),
+                                     kx(_bin("+", k_expr, col))),
                 nbytes=16, swizzle="NONE", lane_index=None, lane_rows=0))
         for i in range((BKs * TN // 4) // T):
             flat = _bin("*", _bin("+", lin, _lit(i * T)), _lit(4))
             row, col = _bin("/", flat, _lit(TN)), _bin("%", flat, _lit(TN))
             out.append(CpAsyncCopy(
                 smem="_b_smem", smem_index=(_bin("+", _bin("*", stage_expr, _lit(BKs)), row), col),
-                src="x1", src_index=(_bin("+", k_expr, row),
+                src="x1", src_index=(kx(_bin("+", k_expr, row)),
                                      _bin("+", _bin("*", a1b, _lit(TN)), col)),
                 nbytes=16, swizzle="NONE", lane_index=None, lane_rows=0))
         out.append(CpAsyncCommit())
@@ -377,7 +390,7 @@ def matmul(M=4096, N=4096, K=4096, TM=128, TN=256, RM=8, RN=16, BKs=32, S=4, std
         stmts += copies(_lit(st), _lit(st * BKs))
     kb = _bin("/", ks, _lit(BKs))
     ahead = _bin("+", ks, _lit((S - 1) * BKs))
-    k_next = TernaryExpr(cond=_bin("<", ahead, _lit(K)), if_true=ahead, if_false=_lit(K - BKs))
+    k_next = TernaryExpr(cond=_bin("<", ahead, _lit(Kp)), if_true=ahead, if_false=_lit(Kp - BKs))
     stage_next = _bin("%", _bin("+", kb, _lit(S - 1)), _lit(S))
     stage_cur = _bin("%", kb, _lit(S))
     ki = Var(name="_ki")
@@ -401,7 +414,7 @@ def matmul(M=4096, N=4096, K=4096, TM=128, TN=256, RM=8, RN=16, BKs=32, S=4, std
         Loop(axis=Axis(name="_ki", extent=Dim(BKs), window=None), body=tuple(inner),
              unroll=True, seed=False),
         Sync(barrier_id=0, count=None, warp=False)]
-    stmts.append(StridedLoop(axis=Axis(name="_ks", extent=Dim(K), window=None), start=_lit(0),
+    stmts.append(StridedLoop(axis=Axis(name="_ks", extent=Dim(Kp), window=None), start=_lit(0),
                              step=_lit(BKs), body=tuple(body), unroll=False, end=None, seed=True))
     for i in range(RM):
         stmts.append(Write(output="matmul",
@@ -409,7 +422,7 @@ def matmul(M=4096, N=4096, K=4096, TM=128, TN=256, RM=8, RN=16, BKs=32, S=4, std
                                                  _bin("*", a0u, _lit(RM))), _lit(i)),
                                   _bin("+", _bin("*", a1b, _lit(TN)), _bin("*", a1u, _lit(RN)))),
                            values=tuple(f"acc0__c{i}_{j}" for j in range(RN)), value_dtype=F32T,
-                           atomic=False, swizzle="NONE"))
+                           atomic=splits > 1, swizzle="NONE"))
     axes = (Axis(name="a0_b", extent=Dim(M // TM),
                  window=Window(parent=Axis(name="a0", extent=Dim(M), window=None), base=None,
                                bound=None, partition=False)),
@@ -418,6 +431,8 @@ def matmul(M=4096, N=4096, K=4096, TM=128, TN=256, RM=8, RN=16, BKs=32, S=4, std
                                bound=None, partition=False)),
             Axis(name="a0_u", extent=Dim(tu_m), window=None),
             Axis(name="a1_u", extent=Dim(tu_n), window=None))
+    if splits > 1:
+        axes = (Axis(name="_a2_ks", extent=Dim(splits), window=None),) + axes
     tile = Tile(axes=axes, body=tuple(stmts), block_threads=T, aux_threads=0,
                 raster_axes=("a0_b", "a1_b"), raster_group=None, raster_orient="m")
     std = K ** -0.5 if std is None else std
@@ -425,11 +440,12 @@ def matmul(M=4096, N=4096, K=4096, TM=128, TN=256, RM=8, RN=16, BKs=32, S=4, std
             {"name": "x0", "dtype": "f32", "shape": [M, K], "seed": 0, "dist": ["normal", 0.0, std]},
             {"name": "matmul", "dtype": "f32", "shape": [M, N], "output": True}]
     smem = 4 * S * (TM * BKs + BKs * TN)
-    grid = (M // TM) * (N // TN)
+    grid = splits * (M // TM) * (N // TN)
     return _package("k_matmul_tc", "matmul", tile, [("x0", (M, K)), ("x1", (K, N))], [],
                     "matmul", (M, N), args, [grid, 1, 1], [T, 1, 1],
                     f"x0 @ x1  # x0: f32[{M},{K}], x1: f32[{K},{N}]", 1e-4, 1e-4,
-                    smem_bytes=smem if smem > 48 * 1024 else 0, graph_inputs=["x0", "x1"])
+                    smem_bytes=smem if smem > 48 * 1024 else 0, graph_inputs=["x0", "x1"],
+                    zero_outputs=("matmul",) if splits > 1 else ())
 
 
 WORKLOADS.update({

@@ -156,8 +156,14 @@ int emmy_rt_host_free(void *ptr);
  * EMMY_RT_NOALLOC_MAX_CTAS CTAs are accepted; larger grids return
  * EMMY_RT_EINVAL with a message. The call allocates nothing. All calls on a
  * device share that array: calls that overlap on the GPU race and must be
- * serialised. The first call on a device looks up the array's address
- * (cudaGetSymbolAddress); make that first call before any stream capture. */
+ * serialised. x and out must be 4-byte aligned, else EMMY_RT_EINVAL before
+ * any launch. The first call on a device looks up the array's address
+ * (cudaGetSymbolAddress); under CUDA's lazy module loading (the default since
+ * CUDA 12.2) that first call also loads this code and its array onto the
+ * device, so make it before the host's pool reserves the device's memory and
+ * before any stream capture. Later calls outside capture look the address up
+ * again (a reset context is picked up); calls on a capturing stream reuse the
+ * last address found. */
 #define EMMY_RT_NOALLOC_MAX_CTAS 4096
 int emmy_rt_sum_f32_noalloc(uint64_t x, uint64_t n, uint64_t out, uint32_t grid,
                             uint64_t stream);

@@ -30,6 +30,20 @@ def reduce_step(x):
     return x.sum(), x.mean()
 
 
+def reduce_rate(x, seconds: float):
+    """Seconds per ``reduce_step(x)``, averaged over as many back-to-back steps as fit in
+    ``seconds`` (at least 3), after one untimed step. Returns (seconds per step, steps)."""
+    reduce_step(x)
+    t_end = time.perf_counter() + seconds
+    n, t = 0, 0.0
+    while time.perf_counter() < t_end or n < 3:
+        t0 = time.perf_counter()
+        reduce_step(x)
+        t += time.perf_counter() - t0
+        n += 1
+    return t / n, n
+
+
 def time_steps(fn, steps: int, warmup: int = 1):
     for _ in range(warmup):
         fn()

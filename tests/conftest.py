@@ -32,3 +32,18 @@ def gpu_runtime():
     from emmyptx import runtime
     runtime.init(0)
     return runtime
+
+
+def pytest_terminal_summary(terminalreporter):
+    """The largest errors each parity check saw against its bound (tests/tolerance.py); with
+    EMMY_TOLERANCE_REPORT set, also written there as JSON."""
+    import tolerance
+    lines = tolerance.report_lines()
+    if not lines:
+        return
+    terminalreporter.section("parity errors against fp64 (largest per check)")
+    for line in lines:
+        terminalreporter.write_line(line)
+    out = os.environ.get("EMMY_TOLERANCE_REPORT")
+    if out:
+        Path(out).write_text(json.dumps(tolerance.RECORD, indent=1, sort_keys=True))

@@ -2,12 +2,13 @@
 
 Run once in a container that has the reference checkout:
 
-    python tests/golden/make_fixtures.py /root/reference/problems
+    python tests/golden/make_fixtures.py <reference checkout>/problems
 
 For every problem folder it copies the Kernel IR (``*.ir.json``), the launch
 record (``meta.json``) and the golden outputs (``expected.npz``). These are
 data, not code: Emmy's CUDA renderings (``*.ref.cu``) are not copied. The
-GPU box has no reference checkout, so tests read these copies only.
+tests read these copies only, so a machine that runs them needs no
+reference checkout.
 
 It then checks that the oracle's fp64 expressions reproduce every
 ``expected.npz`` array byte for byte from the seeded inputs, which pins the
@@ -55,4 +56,6 @@ def main(src: str) -> int:
 
 
 if __name__ == "__main__":
-    sys.exit(main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/problems"))
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: python {sys.argv[0]} <reference checkout>/problems")
+    sys.exit(main(sys.argv[1]))

@@ -1,10 +1,10 @@
 """Generate the reference-PTX goldens: the reference compiler's own PTX for every fixture and
 for the benchmark configurations in the forms its lowerers accept.
 
-Run in a container that has the reference checkout (the GPU box has none; tests read the
-committed PTX):
+Run where the reference checkout is present (the tests read the committed PTX, so a machine
+that runs them needs no checkout):
 
-    python tests/golden/make_ref_ptx.py /root/reference/compile.py
+    python tests/golden/make_ref_ptx.py <reference checkout>/compile.py
 
 emmy-ml is not installable offline, so the reference runs against the stand-in package in
 ``emmy_stub`` (``Graph.from_dict`` backed by this project's decoder). Outputs go to
@@ -98,4 +98,6 @@ def main(compile_py: str) -> int:
 
 
 if __name__ == "__main__":
-    sys.exit(main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/compile.py"))
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: python {sys.argv[0]} <reference checkout>/compile.py")
+    sys.exit(main(sys.argv[1]))

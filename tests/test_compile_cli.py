@@ -96,7 +96,24 @@ def test_reduction_uses_cross_cta_finish():
     assert template == "rowreduce"
     assert "atom.acq_rel.gpu.global.inc.u32" in ptx
     assert ptx.count("shfl.sync.bfly.b32") >= 5
-    assert ".global .align 16 .f32 emmy_partials" in ptx
+    assert ".global .align 16 .f64 emmy_partials64" in ptx
+
+
+def test_sums_accumulate_in_f64():
+    """Sums (full sum and mean, row sums) widen every element and add in f64, in the
+    per-thread loop and in every fold; the fused row operations (their statistics have no
+    cancellation) keep f32."""
+    from emmyptx import workloads
+    from emmyptx.emit import compile_payload
+    for payload, meta in (workloads.full_reduce(1 << 20, "sum", grid=64),
+                          workloads.full_reduce(1 << 20, "mean", grid=64),
+                          workloads.row_op("rowsum", rows=4, cols=512)):
+        ptx, _, _ = compile_payload(payload, meta)
+        assert "cvt.f64.f32" in ptx and "add.rn.f64" in ptx and "cvt.rn.f32.f64" in ptx
+        assert "shfl.sync.bfly.b32" in ptx and "ld.shared.f64" in ptx
+    for kind in ("rmsnorm", "softmax", "l2norm"):
+        ptx, _, _ = compile_payload(*workloads.row_op(kind, rows=4, cols=512))
+        assert ".f64" not in ptx and "cvt.f64" not in ptx
 
 
 def test_single_cta_reduction_skips_the_ticket():

@@ -1,23 +1,22 @@
 """Attention on B200: the tcgen05 flash template against the fp64 oracle, through the C ABI.
 
-Tolerance (written here): |got - ref| <= 1e-4 * |ref| + 1e-4 * max|ref| against
-``softmax(q @ kt / c) @ v`` computed in float64 (3xTF32 products, f32 softmax).
+Tolerance (written here): |got - ref| <= 1e-4 * |ref| + 1e-4 * max_row|ref| against
+``softmax(q @ kt / c) @ v`` computed in float64 (3xTF32 products, f32 softmax), the maximum
+taken over each query row's output vector (tests/tolerance.py:rowscaled).
 """
 
 import numpy as np
 import pytest
+
+import tolerance as tol
 
 pytestmark = pytest.mark.gpu
 
 REL = 1e-4
 
 
-def _close(got, ref, rel=REL):
-    ref = np.asarray(ref, dtype=np.float64)
-    got = np.asarray(got, dtype=np.float64).reshape(ref.shape)
-    scale = float(np.max(np.abs(ref)))
-    ok = np.abs(got - ref) <= rel * np.abs(ref) + rel * scale
-    return bool(np.all(ok)), float(np.max(np.abs(got - ref)) / max(scale, 1e-30))
+def _close(got, ref, rel=REL, label=None):
+    return tol.rowscaled(got, ref, rel, label=label)
 
 
 def _ref_heads(inputs, heads):
@@ -44,15 +43,19 @@ def _run(gpu_runtime, payload, meta, template=None, grid=None):
 
 @pytest.mark.parametrize("name", ["attention_d128", "attention_d64"])
 def test_attention_full_size(name, gpu_runtime):
-    """[8,16,2048,D] on tcgen05: every value finite, sampled heads within 1e-4 of fp64."""
+    """[8,16,2048,D] on tcgen05: all 8 x 16 heads within 1e-4 of fp64 (the fp64 result is
+    computed one batch entry, 16 heads, at a time)."""
     from emmyptx import workloads
+    from oracle.expressions import _attention
     payload, meta = workloads.WORKLOADS[name]()
     used, inputs, got = _run(gpu_runtime, payload, meta)
     assert used == "attention"
     assert np.all(np.isfinite(got))
-    heads = [(0, 0), (3, 7), (7, 15)]
-    ok, err = _close(np.stack([got[b, h] for b, h in heads]), _ref_heads(inputs, heads))
-    assert ok, f"relative error {err:.3e}"
+    c = float(inputs["div_c1"][0])
+    for b in range(got.shape[0]):
+        want = _attention(inputs["q"][b], inputs["kt"][b], inputs["v"][b], c)
+        ok, err = _close(got[b], want, label=f"config {name}")
+        assert ok, f"batch entry {b}: error {err:.3e} of the row maximum"
 
 
 @pytest.mark.parametrize("shape", [(1, 2, 256, 128, None), (2, 1, 384, 64, None),
@@ -69,11 +72,11 @@ def test_attention_template_matches_fp64_and_walker(shape, gpu_runtime):
     assert used == "attention"
     heads = [(b, h) for b in range(B) for h in range(H)]
     want = _ref_heads(inputs, heads).reshape(got.shape)
-    ok, err = _close(got, want)
+    ok, err = _close(got, want, label="attention small tcgen05")
     assert ok, f"template relative error {err:.3e}"
     used_w, _, got_w = _run(gpu_runtime, payload, meta, template="walker")
     assert used_w == "walker"
-    ok, err = _close(got_w, want)
+    ok, err = _close(got_w, want, label="attention small walker")
     assert ok, f"walker relative error {err:.3e}"
 
 
@@ -117,5 +120,5 @@ def test_attention_warp_template_matches_fp64(form, args, grid, gpu_runtime):
     else:
         B, H = args[0], args[1]
         want = _ref_heads(inputs, [(b, h) for b in range(B) for h in range(H)])
-    ok, err = _close(got, np.asarray(want).reshape(got.shape))
+    ok, err = _close(got, np.asarray(want).reshape(got.shape), label="attention warp-per-row")
     assert ok, f"relative error {err:.3e}"

@@ -9,7 +9,10 @@ scalar sum, 128-thread row kernels, the rank-2 attention slice).
 Tolerances (written here): pointwise bit-exact; reductions and row operations
 |ours - ref| <= 1e-5 * |ref| + 1e-5 * max|ref|; matmul and attention the same with 1e-4. The
 reference output is itself checked against the fp64 oracle with the same bound, so a
-disagreement points at one side.
+disagreement points at one side. Both compilers' outputs carry their own f32 rounding (the
+reference's grid-1 sum adds 2^18 terms per thread in sequence), so the two are compared in
+this max-scaled form; the element-wise bounds against fp64 that our kernels are held to are in
+test_gpu_parity.py and test_gpu_attention.py.
 """
 
 import json

@@ -98,7 +98,8 @@ def _fp64(info, inputs):
 
 def test_contraction_tc_covers_every_template_form():
     """synth.contraction_tc's first 32 seeds include single-CTA kernels, CTA pairs, and pairs
-    with half-width units, and every one assembles for sm_100a."""
+    with half-width units, single and pair forms with the split-K atomic epilogue, and every
+    one assembles for sm_100a."""
     import shutil
     import subprocess
     import tempfile
@@ -116,10 +117,13 @@ def test_contraction_tc_covers_every_template_form():
             if "$L_khalf" in ptx:
                 form += "+half"
             forms.add(form)
+            if "red.global.add.f32" in ptx:
+                assert meta["kernels"][0]["zero_outputs"] == ["matmul"]
+                forms.add(form.split("+")[0] + "+atomic")
             if shutil.which("ptxas") and seed < 4:
                 f = Path(tmp) / "k.ptx"
                 f.write_text(ptx)
                 r = subprocess.run(["ptxas", "-arch=sm_100a", "-o", str(Path(tmp) / "k.cubin"),
                                     str(f)], capture_output=True, text=True)
                 assert r.returncode == 0, r.stderr
-    assert forms == {"single", "pair", "pair+half"}
+    assert forms == {"single", "pair", "pair+half", "single+atomic", "pair+atomic"}

@@ -56,4 +56,27 @@ def test_noalloc_sum_matches_emitted_kernel_twice(gpu_runtime):
     # a grid beyond the fixed scratch is refused with a message, nothing launched
     rc = L.emmy_rt_sum_f32_noalloc(xbuf.ptr, n, out_na.ptr, 4097, 0)
     assert rc == -3 and b"outside 1..4096" in L.emmy_rt_last_error()
+    # so is a pointer that is not 4-byte aligned (it would fault in the kernel)
+    rc = L.emmy_rt_sum_f32_noalloc(xbuf.ptr + 2, n - 1, out_na.ptr, grid, 0)
+    assert rc == -3 and b"4-byte aligned" in L.emmy_rt_last_error()
     mod.close()
+
+
+@pytest.mark.parametrize("grid", [1, 37])
+def test_noalloc_sum_unaligned_input_and_single_cta(grid, gpu_runtime):
+    """x 4 bytes past a 16-byte boundary takes the kernel's scalar path; one CTA finishes
+    alone (its ticket wraps at once). Two calls in a row, both within 1e-5 of fp64."""
+    rt = gpu_runtime
+    n = 100_003
+    x = np.random.default_rng(12).uniform(-1, 1, n).astype(np.float32)
+    exact = float(x.astype(np.float64).sum())
+    xbuf = rt.DeviceBuffer.from_array(np.concatenate([np.zeros(1, np.float32), x]))
+    out = rt.DeviceBuffer(4)
+    L = rt.lib()
+    for _ in range(2):
+        out.zero()
+        rc = L.emmy_rt_sum_f32_noalloc(xbuf.ptr + 4, n, out.ptr, grid, 0)
+        assert rc == 0, L.emmy_rt_last_error()
+        rt.sync()
+        got = float(out.download(np.zeros(1, np.float32))[0])
+        assert abs(got - exact) <= REL * abs(exact), (got, exact)
