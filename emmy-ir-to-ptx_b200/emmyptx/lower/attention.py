@@ -38,7 +38,7 @@ from __future__ import annotations
 
 from math import gcd
 
-from .common import WAIT_LIMIT, tf32_split
+from .common import WAIT_LIMIT, pack2, tf32_split_pairs, unpack2
 
 TQ = 128
 BKV = 64
@@ -172,10 +172,10 @@ class _TileCopy:
         for i, four in enumerate(regs):
             b = self.bases[i % self.P]
             imm = (i // self.P) * step
-            parts = [tf32_split(gen, x) for x in four]
+            his, los = tf32_split_pairs(gen, four)
             pred = f"@{self.pv} " if (self.pv and i == self.iters - 1) else ""
-            gen.emit(f"{pred}st.shared.v4.b32 [{b}+{imm + hi}], {{{', '.join(p[0] for p in parts)}}};")
-            gen.emit(f"{pred}st.shared.v4.b32 [{b}+{imm + lo}], {{{', '.join(p[1] for p in parts)}}};")
+            gen.emit(f"{pred}st.shared.v4.b32 [{b}+{imm + hi}], {{{', '.join(his)}}};")
+            gen.emit(f"{pred}st.shared.v4.b32 [{b}+{imm + lo}], {{{', '.join(los)}}};")
 
 
 def _item_loop(gen, cta, ncta, nitems, hint):
@@ -224,6 +224,45 @@ def _parity(gen, counter, shift=0, minus=0):
         src = r
     gen.emit(f"and.b32 {r}, {src}, 1;")
     return r
+
+
+def _tree3(gen, op, regs):
+    """Reduction of ``regs`` with the three-input f32 ``min``/``max`` (``op`` is
+    ``max.f32`` or ``min.f32``): about half the instructions of a pairwise tree."""
+    level = list(regs)
+    while len(level) > 1:
+        nxt = []
+        i = 0
+        while i < len(level):
+            chunk = level[i:i + 3]
+            if len(chunk) == 1:
+                nxt.append(chunk[0])
+            else:
+                t = gen.register(".f32")
+                gen.emit(f"{op} {t}, {', '.join(chunk)};")
+                nxt.append(t)
+            i += 3
+        level = nxt
+    return level[0]
+
+
+def _sum_pairs(gen, regs):
+    """Sum of an even number of f32 registers: a pairwise tree over packed pairs
+    (``add.rn.f32x2``), then one add of the two lanes."""
+    level = [pack2(gen, a, b) for a, b in zip(regs[0::2], regs[1::2])]
+    while len(level) > 1:
+        nxt = []
+        for a, b in zip(level[0::2], level[1::2]):
+            t = gen.register(".b64")
+            gen.emit(f"add.rn.f32x2 {t}, {a}, {b};")
+            nxt.append(t)
+        if len(level) % 2:
+            nxt.append(level[-1])
+        level = nxt
+    x, y = unpack2(gen, level[0])
+    t = gen.register(".f32")
+    gen.emit(f"add.rn.f32 {t}, {x}, {y};")
+    return t
 
 
 def _tree(gen, op, regs):
@@ -395,6 +434,7 @@ def _softmax_role(gen, ptr, plan, tid, warp, tmem, base, B, wait, cta, ncta, c):
     gen.emit(f"mul.rn.f32 {scale}, {scale}, 0f3FB8AA3B;")
     p_neg = gen.register(".pred")
     gen.emit(f"setp.lt.f32 {p_neg}, {scale}, 0f00000000;")
+    scale2 = pack2(gen, scale, scale)
     # P row base addresses for the 8 swizzle phases: row*128 + ((k/4 % 8) ^ row % 8) * 16
     r8, prow = gen.register(".u32"), gen.register(".u32")
     gen.emit(f"and.b32 {r8}, {tid}, 7;")
@@ -429,7 +469,7 @@ def _softmax_role(gen, ptr, plan, tid, warp, tmem, base, B, wait, cta, ncta, c):
 
     def q_store(regs):
         for cb in range(D // 32):
-            his, los = zip(*[tf32_split(gen, x) for x in regs[cb * 32:cb * 32 + 32]])
+            his, los = tf32_split_pairs(gen, regs[cb * 32:cb * 32 + 32])
             gen.emit(f"tcgen05.st.sync.aligned.32x32b.x32.b32 [{trow}+{c['QHI'] + cb * 32}], "
                      f"{{{', '.join(his)}}};")
             gen.emit(f"tcgen05.st.sync.aligned.32x32b.x32.b32 [{trow}+{c['QLO'] + cb * 32}], "
@@ -499,10 +539,10 @@ def _softmax_role(gen, ptr, plan, tid, warp, tmem, base, B, wait, cta, ncta, c):
         mx = gen.register(".f32")
         L_min, L_mx = gen.new_label("smin"), gen.new_label("smx")
         gen.emit(f"@{p_neg} bra.uni {L_min};")
-        gen.emit(f"mov.f32 {mx}, {_tree(gen, 'max.f32', s)};")
+        gen.emit(f"mov.f32 {mx}, {_tree3(gen, 'max.f32', s)};")
         gen.emit(f"bra.uni {L_mx};")
         gen.label(L_min)
-        gen.emit(f"mov.f32 {mx}, {_tree(gen, 'min.f32', s)};")
+        gen.emit(f"mov.f32 {mx}, {_tree3(gen, 'min.f32', s)};")
         gen.label(L_mx)
         gen.emit(f"mul.rn.f32 {mx}, {mx}, {scale};")
         thr, need, anyneed = gen.register(".f32"), gen.register(".pred"), gen.register(".pred")
@@ -541,13 +581,16 @@ def _softmax_role(gen, ptr, plan, tid, warp, tmem, base, B, wait, cta, ncta, c):
         gen.emit(f"neg.f32 {negm}, {m_used};")
         # ex2 without subnormal handling: arguments are at most 8 (the lazy maximum), and a
         # score below 2^-126 of the row's maximum weighs nothing next to it
+        # two scores per fma.rn.f32x2 (each lane rounded as fma.rn.f32 would)
+        negm2 = pack2(gen, negm, negm)
         p = []
-        for x in s:
-            t = gen.register(".f32")
-            gen.emit(f"fma.rn.f32 {t}, {x}, {scale}, {negm};")
-            gen.emit(f"ex2.approx.ftz.f32 {t}, {t};")
-            p.append(t)
-        gen.emit(f"add.rn.f32 {lsum}, {lsum}, {_tree(gen, 'add.rn.f32', p)};")
+        for x, y in zip(s[0::2], s[1::2]):
+            t2 = gen.register(".b64")
+            gen.emit(f"fma.rn.f32x2 {t2}, {pack2(gen, x, y)}, {scale2}, {negm2};")
+            for t in unpack2(gen, t2):
+                gen.emit(f"ex2.approx.ftz.f32 {t}, {t};")
+                p.append(t)
+        gen.emit(f"add.rn.f32 {lsum}, {lsum}, {_sum_pairs(gen, p)};")
         # P -> shared memory once P*V of the previous block has released it
         L_nopw = gen.new_label("nopw")
         pz = gen.register(".pred")
@@ -557,18 +600,18 @@ def _softmax_role(gen, ptr, plan, tid, warp, tmem, base, B, wait, cta, ncta, c):
         gen.label(L_nopw)
         if c["P_TMEM"]:
             for cb in range(BKV // 32):
-                his, los = zip(*[tf32_split(gen, x) for x in p[cb * 32:cb * 32 + 32]])
+                his, los = tf32_split_pairs(gen, p[cb * 32:cb * 32 + 32])
                 for col, regs in ((c["PTHI"], his), (c["PTLO"], los)):
                     gen.emit(f"tcgen05.st.sync.aligned.32x32b.x32.b32 [{trow}+{col + cb * 32}], "
                              f"{{{', '.join(regs)}}};")
             gen.emit("tcgen05.wait::st.sync.aligned;")
         else:
             for k4 in range(BKV // 4):
-                parts = [tf32_split(gen, x) for x in p[4 * k4:4 * k4 + 4]]
+                halves = tf32_split_pairs(gen, p[4 * k4:4 * k4 + 4])
                 atom = (4 * k4) // 32
-                for nm, idx in (("PHI", 0), ("PLO", 1)):
+                for nm, regs in zip(("PHI", "PLO"), halves):
                     gen.emit(f"st.shared.v4.b32 [{pofs[k4 % 8]}+{c[nm] + atom * TQ * 128}], "
-                             f"{{{', '.join(pp[idx] for pp in parts)}}};")
+                             f"{{{', '.join(regs)}}};")
             gen.emit("fence.proxy.async.shared::cta;")
         gen.emit("tcgen05.fence::before_thread_sync;")
         gen.emit(f"mbarrier.arrive.shared::cta.b64 _, [{B['PVGO']}];")

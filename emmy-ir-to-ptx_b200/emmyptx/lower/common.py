@@ -53,3 +53,32 @@ def tf32_split(gen, x) -> tuple:
     lo = gen.register(".f32")
     gen.emit(f"sub.rn.f32 {lo}, {x}, {h};")
     return h, lo
+
+
+def pack2(gen, a, b) -> str:
+    """The f32 pair (a, b) as one .b64 register (operand of the packed .f32x2 instructions)."""
+    d = gen.register(".b64")
+    gen.emit(f"mov.b64 {d}, {{{a}, {b}}};")
+    return d
+
+
+def unpack2(gen, d) -> tuple:
+    a, b = gen.register(".f32"), gen.register(".f32")
+    gen.emit(f"mov.b64 {{{a}, {b}}}, {d};")
+    return a, b
+
+
+def tf32_split_pairs(gen, xs) -> tuple:
+    """:func:`tf32_split` of an even number of registers, the subtraction done two elements
+    per instruction (``sub.rn.f32x2``, rounded per element exactly as ``sub.rn.f32``)."""
+    his, los = [], []
+    for x, y in zip(xs[0::2], xs[1::2]):
+        hx, hy = gen.register(".b32"), gen.register(".b32")
+        gen.emit(f"and.b32 {hx}, {x}, -8192;")
+        gen.emit(f"and.b32 {hy}, {y}, -8192;")
+        d = gen.register(".b64")
+        gen.emit(f"sub.rn.f32x2 {d}, {pack2(gen, x, y)}, {pack2(gen, hx, hy)};")
+        lx, ly = unpack2(gen, d)
+        his += [hx, hy]
+        los += [lx, ly]
+    return his, los
