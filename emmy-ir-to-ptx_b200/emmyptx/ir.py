@@ -306,10 +306,28 @@ def _fast_build(data):
     return build(data)
 
 
+try:  # the native decoder (csrc/emmy_irdecode.c), built in-tree by __graft_entry__.build()
+    from . import _irdecode as _native
+    _native.setup(_CLASSES, NODE_FIELDS, _DEFAULTS, IRDecodeError)
+except ImportError:
+    _native = None
+
+
 def decode_statement(text: str):
-    """Decode one statement repr string into IR nodes."""
+    """Decode one statement repr string into IR nodes.
+
+    The native decoder reads the grammar in one pass when it is built; on anything it does
+    not cover, and on any error, the statement is decoded again here (the JSON fast path,
+    else :func:`ast.parse`), so results and error messages are the Python decoders'."""
     if not isinstance(text, str):
         raise IRDecodeError("KernelOp body entries must be strings")
+    if _native is not None:
+        try:
+            value = _native.decode(text)
+        except Exception:           # noqa: BLE001 - Fallback, or an error the paths below name
+            value = None
+        if isinstance(value, Node) and type(value).__name__ in STATEMENT_KINDS:
+            return value
     fast = _fast_json(text)
     if fast is not None:
         try:

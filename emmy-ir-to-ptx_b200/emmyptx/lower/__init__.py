@@ -31,10 +31,10 @@ MIN_CONTRACTION_MACS = 1 << 22
 
 
 def _fits_contraction(kernel, forced=False):
-    from .matmul import plan_tiles
     plan = lift_contraction(kernel)
     if plan is None or (not forced and plan.M * plan.N * plan.K < MIN_CONTRACTION_MACS):
         return None
+    from .matmul import plan_tiles      # the template module only once the body lifted
     block = list(kernel.launch.get("block", [1, 1, 1]))
     if block[1:] != [1, 1] or list(kernel.launch.get("grid", [1, 1, 1]))[1:] != [1, 1]:
         return None
@@ -45,19 +45,19 @@ def _fits_contraction(kernel, forced=False):
 
 
 def _fits_attention(kernel):
-    from .attention import fits
     plan = lift_attention(kernel)
-    if plan is None or not fits(plan, kernel.launch):
+    if plan is None:
         return None
-    return plan
+    from .attention import fits
+    return plan if fits(plan, kernel.launch) else None
 
 
 def _fits_attention_warp(kernel):
-    from .attention_warp import fits
     plan = lift_attention(kernel)
-    if plan is None or not fits(plan, kernel.launch):
+    if plan is None:
         return None
-    return plan
+    from .attention_warp import fits
+    return plan if fits(plan, kernel.launch) else None
 
 
 _EMITTERS = {"matmul": "lower_contraction", "attention": "lower_attention",

@@ -41,13 +41,17 @@ from math import gcd
 from .common import WAIT_LIMIT, pack2, tf32_split_pairs, unpack2
 
 TQ = 128
-BKV = 64
+# keys per block: 64 at D = 64; 32 at D = 128, where the tensor memory then also holds P
+# (Q hi/lo 256 + two S buffers 64 + O 128 + P hi/lo 64 = 512 columns), so P*V reads A from
+# tensor memory and P never goes through shared memory
+BKV_FOR_D = {64: 64, 128: 32}
 THREADS = 256
 NLOAD = 96                 # loader threads: warps 5-7
 RESCALE_BITS = "0f41000000"   # 8.0: raise the running maximum only past 2^8 of growth
 
 
 def smem_bytes_needed(D):
+    BKV = BKV_FOR_D[D]
     return 2 * (D * BKV * 4) * 2 + 2 * (TQ * BKV * 4)
 
 
@@ -58,7 +62,7 @@ def fits(plan, launch):
         return False
     if plan.D not in (64, 128) or plan.Dv != plan.D:
         return False
-    if plan.Sq % TQ or plan.Skv % BKV:
+    if plan.Sq % TQ or plan.Skv % BKV_FOR_D[plan.D]:
         return False
     return int(launch.get("smem_bytes", 0) or 0) >= smem_bytes_needed(plan.D)
 
@@ -291,7 +295,8 @@ def _pair_barrier(gen, B, first, counter):
 
 def lower_attention(gen, kernel, plan):
     D = plan.D
-    c = dict(D=D, NB=plan.Skv // BKV, NQB=plan.Sq // TQ, Sq=plan.Sq, Skv=plan.Skv)
+    BKV = BKV_FOR_D[D]
+    c = dict(D=D, BKV=BKV, NB=plan.Skv // BKV, NQB=plan.Sq // TQ, Sq=plan.Sq, Skv=plan.Skv)
     c["NITEMS"] = plan.G * c["NQB"]
     # tensor memory columns: Q_hi, Q_lo, two S buffers, the O accumulator
     c.update(QHI=0, QLO=D, S0=2 * D, O=2 * D + 2 * BKV)
@@ -421,6 +426,7 @@ def lower_attention(gen, kernel, plan):
 # ------------------------------------------------------------------ softmax warps 0-3
 
 def _softmax_role(gen, ptr, plan, tid, warp, tmem, base, B, wait, cta, ncta, c):
+    BKV = c["BKV"]
     D, NB, NQB = c["D"], c["NB"], c["NQB"]
     lane_field = gen.register(".u32")
     gen.emit(f"shl.b32 {lane_field}, {warp}, 21;")
@@ -645,6 +651,7 @@ def _softmax_role(gen, ptr, plan, tid, warp, tmem, base, B, wait, cta, ncta, c):
 # ------------------------------------------------------------------ MMA warp 4
 
 def _mma_role(gen, tmem, base, B, wait, cta, ncta, lane, c):
+    BKV = c["BKV"]
     D, NB = c["D"], c["NB"]
     p_el, el = gen.register(".pred"), gen.register(".u32")
     gen.emit(f"elect.sync {el}|{p_el}, -1;")
@@ -764,7 +771,7 @@ def _load_role(gen, ptr, plan, tid, base, B, wait, cta, ncta, c):
     while S_(j+1) runs (PV_(j-1) has released the v buffer): the kt tiles are kept one
     block ahead of the v tiles. The global loads of each tile are issued a step before its
     buffer wait, so L2 latency overlaps the tensor-core work."""
-    D, NB, NQB = c["D"], c["NB"], c["NQB"]
+    D, NB, NQB, BKV = c["D"], c["NB"], c["NQB"], c["BKV"]
     lt = gen.register(".u32")
     gen.emit(f"sub.u32 {lt}, {tid}, 160;")
     ktc = _TileCopy(gen, lt, rows=D, cols=BKV, row_stride=c["Skv"], sbo=c["SBO_K"], base=base)

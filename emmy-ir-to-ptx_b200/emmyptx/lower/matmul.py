@@ -46,20 +46,34 @@ BK = 32
 SM_COUNT = 148                   # B200: CTA pairs that run at once = SM_COUNT / 2
 
 
+def _bn_choices(N):
+    """Tile widths to try for N columns, widest first: the widths that divide N, else
+    (ragged N, the last tile masked) every width from the narrowest power of two that covers
+    N (at most 256) down to 32."""
+    exact = [bn for bn in (256, 128, 64, 32) if N % bn == 0]
+    if exact:
+        return exact
+    return [bn for bn in (256, 128, 64, 32) if bn < 2 * N or bn == 32]
+
+
+def ragged_ok(M, N, K):
+    """Shapes the template takes with masked tile edges: any M, N and K multiples of 4 (rows
+    of A, B and C start on 16-byte boundaries, and a 16-byte chunk is all in or all out)."""
+    return M > 0 and N > 0 and K > 0 and N % 4 == 0 and K % 4 == 0
+
+
 def plan_tiles(M, N, K, dyn_smem, threads):
-    """(BN, stages, smem placement) for this launch, or None if the template does not fit."""
-    if M % BM or K % BK or threads < 160 or threads % 32 or threads > 1024:
+    """(BN, stages, smem placement) for this launch, or None if the template does not fit.
+    M need not be a multiple of 128, nor N and K of the tile (``ragged_ok``): the edge tiles
+    load zeros past the matrix and store only what lies inside it."""
+    if not ragged_ok(M, N, K) or threads < 160 or threads % 32 or threads > 1024:
         return None
     budget_dyn = dyn_smem if dyn_smem else 0
-    for bn in (256, 128, 64, 32):
-        if N % bn:
-            continue
+    for bn in _bn_choices(N):
         stage = 2 * BM * BK * 4 + 2 * BK * bn * 4
         if budget_dyn >= 2 * stage:
             return bn, min(budget_dyn // stage, 4), "dynamic"
-    for bn in (256, 128, 64, 32):
-        if N % bn:
-            continue
+    for bn in _bn_choices(N):
         stage = 2 * BM * BK * 4 + 2 * BK * bn * 4
         if budget_dyn >= stage:
             return bn, 1, "dynamic"
@@ -72,12 +86,13 @@ def plan_pair(M, N, K, dyn_smem, threads, grid):
     """(BN, stages) of the CTA-pair variant, or None: two CTAs of a cluster share one
     256 x BN tile with ``tcgen05.mma.cta_group::2``; each holds 128 rows of A and BN/2
     columns of B, so per SM the B loads and stores (and the tensor core's B reads) halve.
-    Needs an even grid (clusters of 2), M % 256, and dynamic shared memory for two stages."""
-    if (grid % 2 or M % (2 * BM) or K % BK or threads < 160 or threads % 32
+    Needs an even grid (clusters of 2), M % 256, and dynamic shared memory for two stages;
+    N and K may be ragged (``ragged_ok``)."""
+    if (grid % 2 or M % (2 * BM) or not ragged_ok(M, N, K) or threads < 160 or threads % 32
             or threads > 1024 or not dyn_smem):
         return None
-    for bn in (256, 128, 64):
-        if N % bn:
+    for bn in _bn_choices(N):
+        if bn < 64:
             continue
         stage = 2 * BM * BK * 4 + 2 * BK * (bn // 2) * 4
         if dyn_smem >= 2 * stage:
@@ -140,9 +155,12 @@ def emit_contraction(gen, kernel, a_buf, b_buf, c_buf, M, N, K, atomic):
     B_BYTES = BK * BNH * 4
     STAGE = 2 * A_BYTES + 2 * B_BYTES
     SBO_B = 16 * BNH                     # stride between 4-row K groups of the B tile
-    KB = K // BK
-    NT_N = N // BN
-    NTILES = (M // (2 * BM if pair else BM)) * NT_N
+    KB = -(-K // BK)
+    NT_N = -(-N // BN)
+    MT = 2 * BM if pair else BM          # rows of C one unit covers
+    NTILES = -(-M // MT) * NT_N
+    # ragged edges (masked): rows of A and C past M, columns of B and C past N, the K tail
+    RAG_M, RAG_N, RAG_K = M % MT != 0, N % BN != 0, K % BK != 0
     # two accumulators of BN columns: the MMAs of a unit run while the epilogue drains the
     # previous unit's
     TMEM_COLS = 32
@@ -290,6 +308,7 @@ def emit_contraction(gen, kernel, a_buf, b_buf, c_buf, M, N, K, atomic):
     # =================================== loader / epilogue warps ==========================
     # per-thread chunk offsets (global byte offset within a tile, shared byte offset)
     a_chunks, b_chunks = [], []
+    a_edge = []                        # per A chunk: (row in the tile, K column in the step)
     for i in range(-(-QA // NL)):
         q = gen.register(".u32")
         gen.emit(f"add.u32 {q}, {tid}, {i * NL};")
@@ -309,12 +328,15 @@ def emit_contraction(gen, kernel, a_buf, b_buf, c_buf, M, N, K, atomic):
         gen.emit(f"mul.wide.u32 {goff}, {t32}, 4;")
         soff = gen.register(".u32")
         sw = gen.register(".u32")
+        kcol = gen.register(".u32")              # the chunk's first K column in the step
+        gen.emit(f"mov.u32 {kcol}, {c};")
         gen.emit(f"shr.u32 {c}, {c}, 2;")
         gen.emit(f"xor.b32 {sw}, {c}, {r8};")
         gen.emit(f"shl.b32 {sw}, {sw}, 4;")
         gen.emit(f"shl.b32 {soff}, {row}, 7;")
         gen.emit(f"add.u32 {soff}, {soff}, {sw};")
         a_chunks.append((goff, soff, pv))
+        a_edge.append((row, kcol))
     # B[K, N] row-major is N-contiguous, so it is stored MN-major in the SWIZZLE_128B_BASE32B
     # layout (the only MN-major layout TF32 operands support): atoms of 32 n x 4 k (512 B), the
     # BN/32 atoms of a 4-row K group side by side (LBO 512 B), K groups SBO_B = 16*BN bytes apart;
@@ -324,7 +346,7 @@ def emit_contraction(gen, kernel, a_buf, b_buf, c_buf, M, N, K, atomic):
         layout of a BNH-wide tile: a narrower tile fills the first cols/32 atoms of each K
         group, so the MMA reads it with the same descriptors and a smaller N."""
         QBc = BK * cols // 4
-        out = []
+        out, edge = [], []
         for i in range(-(-QBc // NL)):
             q = gen.register(".u32")
             gen.emit(f"add.u32 {q}, {tid}, {i * NL};")
@@ -357,10 +379,11 @@ def emit_contraction(gen, kernel, a_buf, b_buf, c_buf, M, N, K, atomic):
             gen.emit(f"mad.lo.u32 {soff}, {u32b}, 32, {soff};")
             gen.emit(f"mad.lo.u32 {soff}, {half}, 16, {soff};")
             out.append((goff, soff, pv))
-        return out
+            edge.append((k, n4))             # (K row in the step, column in the tile)
+        return out, edge
 
-    b_chunks = b_chunk_list(BNH)
-    b_chunks_half = b_chunk_list(BNH // 2) if H else None
+    b_chunks, b_edge = b_chunk_list(BNH)
+    b_chunks_half, b_edge_half = b_chunk_list(BNH // 2) if H else (None, None)
 
     def unit_tile(u):
         """(tile index, which half, is-half predicate) of work unit ``u``: units below F are
@@ -426,23 +449,77 @@ def emit_contraction(gen, kernel, a_buf, b_buf, c_buf, M, N, K, atomic):
     gen.emit(f"mul.wide.u32 {tmp64}, {nb0}, 4;")
     gen.emit(f"add.s64 {b_tile}, {B}, {tmp64};")
 
+    # ragged edges: per unit, which of this thread's chunks lie inside M (A rows) and N (B
+    # columns); the K tail is checked per step in issue_loads
+    tile_ok = {}
+    if RAG_M:
+        tile_ok["a"] = []
+        for row, _ in a_edge:
+            t, q = gen.register(".u32"), gen.register(".pred")
+            gen.emit(f"add.u32 {t}, {m0}, {row};")
+            gen.emit(f"setp.lt.u32 {q}, {t}, {M};")
+            tile_ok["a"].append(q)
+    if RAG_N:
+        for key, edge in (("b", b_edge), ("bh", b_edge_half)):
+            if edge is None:
+                continue
+            tile_ok[key] = []
+            for _, n4 in edge:
+                t, q = gen.register(".u32"), gen.register(".pred")
+                gen.emit(f"add.u32 {t}, {nb0}, {n4};")
+                gen.emit(f"setp.lt.u32 {q}, {t}, {N};")
+                tile_ok[key].append(q)
+
     def issue_loads(kb, regs=None, bch=b_chunks):
-        """Global loads of K step ``kb`` (a register or an int) into ``regs`` (new if None)."""
+        """Global loads of K step ``kb`` (a register or an int) into ``regs`` (new if None).
+        With ragged edges a chunk outside the matrix is zeroed instead of loaded."""
         a_k, b_k = gen.register(".u64"), gen.register(".u64")
+        kk = None
         if isinstance(kb, int):
             gen.emit(f"add.s64 {a_k}, {a_tile}, {kb * BK * 4};")
             gen.emit(f"add.s64 {b_k}, {b_tile}, {kb * BK * N * 4};")
+            if RAG_K:
+                kk = gen.register(".u32")
+                gen.emit(f"mov.u32 {kk}, {kb * BK};")
         else:
             gen.emit(f"mul.wide.u32 {tmp64}, {kb}, {BK * 4};")
             gen.emit(f"add.s64 {a_k}, {a_tile}, {tmp64};")
             gen.emit(f"mul.wide.u32 {tmp64}, {kb}, {BK * N * 4};")
             gen.emit(f"add.s64 {b_k}, {b_tile}, {tmp64};")
+            if RAG_K:
+                kk = gen.register(".u32")
+                gen.emit(f"mul.lo.u32 {kk}, {kb}, {BK};")
         out = regs if regs is not None else [gen.registers(".f32", 4)
                                              for _ in range(len(a_chunks) + len(bch))]
+        nA = len(a_chunks)
+        bkey = "b" if bch is b_chunks else "bh"
+        bedge = b_edge if bch is b_chunks else b_edge_half
         for idx, (goff, soff, pv) in enumerate(a_chunks + bch):
             addr = gen.register(".u64")
-            gen.emit(f"add.s64 {addr}, {a_k if idx < len(a_chunks) else b_k}, {goff};")
-            pred = f"@{pv} " if pv else ""
+            gen.emit(f"add.s64 {addr}, {a_k if idx < nA else b_k}, {goff};")
+            conds = [pv] if pv else []
+            if idx < nA and "a" in tile_ok:
+                conds.append(tile_ok["a"][idx])
+            if idx >= nA and bkey in tile_ok:
+                conds.append(tile_ok[bkey][idx - nA])
+            if RAG_K:
+                kpos = a_edge[idx][1] if idx < nA else bedge[idx - nA][0]
+                t, q = gen.register(".u32"), gen.register(".pred")
+                gen.emit(f"add.u32 {t}, {kk}, {kpos};")
+                gen.emit(f"setp.lt.u32 {q}, {t}, {K};")
+                conds.append(q)
+            masked = len(conds) > (1 if pv else 0)
+            if masked:                       # zeros where the chunk lies outside the matrix
+                for r in out[idx]:
+                    gen.emit(f"mov.f32 {r}, 0f00000000;")
+            pred = ""
+            if conds:
+                q = conds[0]
+                for extra in conds[1:]:
+                    t = gen.register(".pred")
+                    gen.emit(f"and.pred {t}, {q}, {extra};")
+                    q = t
+                pred = f"@{q} "
             gen.emit(f"{pred}ld.global.nc.L1::no_allocate.v4.f32 {{{', '.join(out[idx])}}}, "
                      f"[{addr}];")
         return out
@@ -572,6 +649,14 @@ def emit_contraction(gen, kernel, a_buf, b_buf, c_buf, M, N, K, atomic):
     gen.emit(f"mad.lo.u32 {lane_field}, {ab}, {BN}, {lane_field};")   # + accumulator columns
     gen.emit("bar.warp.sync -1;")
     width = 64 if BN >= 64 else 32
+    # ragged edges: rows past M and 4-column chunks past N are not stored
+    p_rowok = ncols_left = None
+    if RAG_M:
+        p_rowok = gen.register(".pred")
+        gen.emit(f"setp.lt.u32 {p_rowok}, {grow}, {M};")
+    if RAG_N:
+        ncols_left = gen.register(".s32")
+        gen.emit(f"sub.s32 {ncols_left}, {N}, {n0};")
     L_cols_done = gen.new_label("colsdone")
     for cb in range(BN // width):
         if H and cb == (BN // 2) // width:
@@ -585,13 +670,22 @@ def emit_contraction(gen, kernel, a_buf, b_buf, c_buf, M, N, K, atomic):
         for v in range(width // 4):
             four = regs[4 * v:4 * v + 4]
             off = 4 * (cb * width + 4 * v)
+            pred = ""
+            if RAG_N:
+                q = gen.register(".pred")
+                gen.emit(f"setp.gt.s32 {q}, {ncols_left}, {cb * width + 4 * v};")
+                if p_rowok is not None:
+                    gen.emit(f"and.pred {q}, {q}, {p_rowok};")
+                pred = f"@{q} "
+            elif p_rowok is not None:
+                pred = f"@{p_rowok} "
             if atomic:
                 for e, r in enumerate(four):
                     f = gen.register(".f32")
                     gen.emit(f"mov.b32 {f}, {r};")
-                    gen.emit(f"red.global.add.f32 [{crow}+{off + 4 * e}], {f};")
+                    gen.emit(f"{pred}red.global.add.f32 [{crow}+{off + 4 * e}], {f};")
             else:
-                gen.emit(f"st.global.v4.b32 [{crow}+{off}], {{{', '.join(four)}}};")
+                gen.emit(f"{pred}st.global.v4.b32 [{crow}+{off}], {{{', '.join(four)}}};")
     gen.label(L_cols_done)
     gen.emit("tcgen05.fence::before_thread_sync;")
     aeb = gen.register(".u32")

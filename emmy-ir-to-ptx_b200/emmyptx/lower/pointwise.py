@@ -12,6 +12,15 @@ launches with more threads than cells (the Tile-extent guard of reference
 
 The leftover ``E mod 4`` elements, and any call whose buffers are not 16-byte
 aligned, take a scalar path with the same arithmetic.
+
+Overlapped launches: the kernel executes ``griddepcontrol.launch_dependents``
+at entry, so a kernel launched after it with programmatic stream
+serialization (``emmy_rt_launch_ex``, ``EMMY_RT_LAUNCH_OVERLAP``) can be
+scheduled while this one runs, and ``griddepcontrol.wait`` before its first
+global access, so it reads nothing before the previous kernel on the stream
+has completed (a chain of pointwise kernels stays ordered). A small launch is
+dominated by its fixed launch cost; overlapping consecutive launches hides it.
+Under a plain launch both instructions do nothing.
 """
 
 from __future__ import annotations
@@ -27,6 +36,8 @@ def lower_pointwise(gen, kernel, plan) -> None:
     buffers = list(dict.fromkeys(plan.inputs + plan.outputs + [b for b, _ in plan.uniforms]))
     ptrs = load_pointers(gen, [a for a in kernel.arg_order if a in buffers])
     written = set(plan.outputs)
+    gen.emit("griddepcontrol.launch_dependents;")
+    gen.emit("griddepcontrol.wait;")
     ld_elem = "ld.global.v4.f32" if written & set(plan.inputs) else \
         "ld.global.nc.L1::no_allocate.v4.f32"
     ld_scalar = "ld.global.f32" if written & set(plan.inputs) else "ld.global.nc.f32"

@@ -160,6 +160,22 @@ def contraction_tc(seed: int):
     return payload, meta, {"M": M, "N": N, "K": K, "TN": TN, "S": S, "splits": splits}
 
 
+def contraction_ragged(seed: int):
+    """A random matmul whose shape is not a multiple of the tcgen05 template's tile: M not a
+    multiple of 128, N or K not of the template's tile width or K step (N and K multiples of
+    4), from IR schedules whose own tiles do divide the shape (64 x 64, 64 x 16 and
+    128 x 256 tiles with K steps of 32, 64 and 16). Compile with ``template="contraction"``."""
+    rng = random.Random(1000 + seed)
+    TM, TN, RM, RN, BKs = rng.choice([(64, 64, 4, 4, 32), (64, 16, 4, 1, 64),
+                                      (128, 256, 8, 16, 16)])
+    M = TM * rng.randint(1, 6)
+    N = TN * rng.randint(1, 6)
+    K = BKs * rng.randint(1, 6)
+    S = rng.choice([2, 3, 4])
+    payload, meta = workloads.matmul(M, N, K, TM=TM, TN=TN, RM=RM, RN=RN, BKs=BKs, S=S)
+    return payload, meta, {"M": M, "N": N, "K": K, "tile": (TM, TN, RM, RN, BKs), "S": S}
+
+
 def attention(seed: int):
     """A random attention problem, in the a02 fixture's rank-2 form (one query row per CTA,
     walker) or in the tiled form (query blocks of 128 rows; the tcgen05 template when the

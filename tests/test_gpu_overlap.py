@@ -59,3 +59,42 @@ def test_overlapped_sum_mean_match_plain_launches(n, grid):
         assert got[r].tobytes() == got[0].tobytes(), (r, got[r], got[0])
     ms.close()
     mm.close()
+
+
+def test_overlapped_pointwise_chain_stays_ordered():
+    """A chain of overlapped pointwise launches where each kernel reads what the previous one
+    wrote: y_(i+1) = y_i + b for 24 launches. The pointwise kernel waits for its predecessor
+    (``griddepcontrol.wait``) before its first global access, so every step sees the finished
+    previous result; a missing wait would read a stale or half-written y and break the
+    bit-exact match with the same additions done in numpy float32."""
+    from emmyptx import runtime, workloads
+    from emmyptx.emit import compile_payload
+    runtime.init(0)
+    n = (1 << 22) + 12
+    payload, meta = workloads.pointwise_add(n)
+    ptx, template, _ = compile_payload(payload, meta)
+    assert template == "pointwise" and "griddepcontrol.wait" in ptx
+    k = meta["kernels"][0]
+    assert [a["name"] for a in k["args"]] == ["x0", "x1", "add"]
+    rng = np.random.default_rng(5)
+    a = rng.standard_normal(n).astype(np.float32)
+    b = rng.standard_normal(n).astype(np.float32)
+    steps = 24
+    ys = [runtime.DeviceBuffer.from_array(a)] + [runtime.DeviceBuffer(4 * n) for _ in range(2)]
+    bb = runtime.DeviceBuffer.from_array(b)
+    mod = runtime.Module(ptx, k["entry"])
+    src = 0
+    for i in range(steps):
+        dst = 1 + (i % 2)
+        mod.launch(k["grid"], k["block"], 0, [ys[src].ptr, bb.ptr, ys[dst].ptr], overlap=True)
+        src = dst
+    runtime.sync()
+    got = ys[src].download(np.zeros(n, np.float32))
+    want = a.copy()
+    for _ in range(steps):
+        want = want + b
+    assert mod.error_word() == 0
+    assert np.array_equal(got, want)
+    mod.close()
+    for buf in ys + [bb]:
+        buf.free()

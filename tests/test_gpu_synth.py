@@ -99,6 +99,25 @@ def test_contraction_template(seed, gpu_runtime):
 
 
 @pytest.mark.parametrize("seed", range(24))
+def test_contraction_ragged_edges(seed, gpu_runtime):
+    """Shapes that are not multiples of the tcgen05 tile (M of 128, N of the tile width, K of
+    32) on the template, with the edge tiles masked: zero-filled loads past the matrix, no
+    stores past it; every seed is also run twice in a row (stale shared memory from the
+    previous tile would show). Within 1e-4 of fp64, error word 0."""
+    from emmyptx import synth
+    from emmyptx.emit import compile_payload
+    from oracle.expressions import kernel_inputs
+    payload, meta, info = synth.contraction_ragged(seed)
+    k = meta["kernels"][0]
+    ptx, template, _ = compile_payload(payload, meta, template="contraction")
+    assert template == "contraction"
+    inputs = kernel_inputs(k)
+    got = gpu_runtime.run_kernel(ptx, k, inputs, iters=2)[0]["matmul"]
+    want = inputs["x0"].astype(np.float64) @ inputs["x1"].astype(np.float64)
+    assert _close(got, want, 1e-4, label="synth matmul ragged tcgen05"), info
+
+
+@pytest.mark.parametrize("seed", range(24))
 def test_attention(seed, gpu_runtime):
     from emmyptx import synth
     from emmyptx.emit import compile_payload
