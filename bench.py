@@ -549,6 +549,11 @@ def _e2e(runtime, ptx_s, k_s, ptx_m, k_m, local_rank, world, dev, fold=None):
 # ---------------------------------------------------------------------------
 
 TENSOR_DENOM = "bf16_tflops / 2 / 3"   # dense TF32 is half the bf16 rate; 3xTF32 = 3 products
+# workload -> its row in profiles/ncu_traffic.txt (DRAM bytes per launch from one ncu capture)
+TRAFFIC_KEY = {"add": "add_2^20", "sum": "sum_2^26", "mean": "mean_2^26",
+               "rmsnorm": "rmsnorm_8192x4096", "softmax": "softmax_8192x4096",
+               "l2norm": "l2norm_8192x4096", "matmul_sq": "matmul_4096",
+               "matmul_rect": "matmul_8192x2048x4096"}
 
 
 def tf32x3_ceiling(peaks):
@@ -682,16 +687,17 @@ def measure_config(name, args, peaks, l2, flush, *, device=0, compile_repeats=5,
         entry["overlapped"] = ov
     if proc_ms is not None:
         entry["compile_process_ms"] = round(proc_ms, 1)
+    traffic = ncu_traffic(k["entry"], TRAFFIC_KEY.get(name, name))
     if bound == "hbm":
         gbs = work / (us * 1e-6) / 1e9
-        entry["roofline"] = {"bound": "hbm", "algorithmic_bytes": int(work),
+        entry["roofline"] = {"bound": "hbm", "algorithmic_bytes": int(work), "traffic": traffic,
                              "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
                              "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
                              "peak_source": f"{peaks['source']} hbm_gbs (burst copy)"}
     else:
         tfl = work / (us * 1e-6) / 1e12
         ceil = tf32x3_ceiling(peaks)
-        entry["roofline"] = {"bound": "tensor", "algorithmic_flops": work,
+        entry["roofline"] = {"bound": "tensor", "algorithmic_flops": work, "traffic": traffic,
                              "achieved": round(tfl, 2), "peak": round(ceil, 1),
                              "unit": "TFLOP/s", "frac": round(tfl / ceil, 4),
                              "peak_source": f"{peaks['source']} {TENSOR_DENOM}"}
