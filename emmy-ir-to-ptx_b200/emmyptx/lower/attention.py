@@ -51,9 +51,22 @@ NLOAD = 96                 # loader threads: warps 5-7
 RESCALE_BITS = "0f41000000"   # 8.0: raise the running maximum only past 2^8 of growth
 
 
-def smem_bytes_needed(D):
+def _p_in_tmem(D, BKV):
+    return 3 * D + 4 * BKV <= 512
+
+
+def smem_bytes_needed(D, nbuf=1):
+    """Dynamic shared memory of the template: ``nbuf`` kt and v tile pairs (hi and lo each),
+    plus P hi/lo when P does not fit in tensor memory."""
     BKV = BKV_FOR_D[D]
-    return 2 * (D * BKV * 4) * 2 + 2 * (TQ * BKV * 4)
+    tiles = nbuf * 2 * (D * BKV * 4) * 2
+    return tiles + (0 if _p_in_tmem(D, BKV) else 2 * (TQ * BKV * 4))
+
+
+def tile_buffers(D, smem):
+    """kt/v tile buffers: two at D = 64 when the launch's shared memory holds them (a tile can
+    then be stored while the tensor core still reads the other), else one."""
+    return 2 if D == 64 and smem >= smem_bytes_needed(D, 2) else 1
 
 
 def fits(plan, launch):
@@ -100,11 +113,13 @@ class _Wait:
         gen.label(ok)
 
 
-def _mn32_offset(gen, krow, ncol4, sbo):
+def _mn32_offset(gen, krow, ncol4, sbo, lbo=512):
     """Byte offset of the 16-byte chunk (k = krow, n = 4*ncol4 .. +3) in an MN-major
-    SWIZZLE_128B_BASE32B tile whose 4-row K groups are ``sbo`` bytes apart: 32 n x 4 k
-    atoms of 512 bytes side by side along n, the 32-byte units of each 128-byte k row
-    permuted by XOR with k % 4."""
+    SWIZZLE_128B_BASE32B tile: 32 n x 4 k atoms of 512 bytes, ``lbo`` bytes apart along n and
+    ``sbo`` bytes apart along k (4-row groups), the 32-byte units of each 128-byte k row
+    permuted by XOR with k % 4. With ``lbo`` = rows x 128 and ``sbo`` = 512 each 32-wide
+    column strip is one contiguous run of 128-byte rows: the layout a TMA box of 32 columns
+    writes with the 128-byte swizzle of 32-byte atoms."""
     j, c8, unit, half, k4, kq, off = (gen.register(".u32") for _ in range(7))
     gen.emit(f"shr.u32 {j}, {ncol4}, 3;")
     gen.emit(f"and.b32 {c8}, {ncol4}, 7;")
@@ -113,7 +128,7 @@ def _mn32_offset(gen, krow, ncol4, sbo):
     gen.emit(f"and.b32 {k4}, {krow}, 3;")
     gen.emit(f"shr.u32 {kq}, {krow}, 2;")
     gen.emit(f"mul.lo.u32 {off}, {kq}, {sbo};")
-    gen.emit(f"mad.lo.u32 {off}, {j}, 512, {off};")
+    gen.emit(f"mad.lo.u32 {off}, {j}, {lbo}, {off};")
     gen.emit(f"mad.lo.u32 {off}, {k4}, 128, {off};")
     gen.emit(f"xor.b32 {unit}, {unit}, {k4};")
     gen.emit(f"mad.lo.u32 {off}, {unit}, 32, {off};")
@@ -130,7 +145,7 @@ class _TileCopy:
     Global offsets are then immediates, and shared-memory offsets repeat with period
     ``P`` (rows mod 4) up to an immediate: both are set up once per kernel."""
 
-    def __init__(self, gen, lt, *, rows, cols, row_stride, sbo, base):
+    def __init__(self, gen, lt, *, rows, cols, row_stride, sbo, base, lbo=512):
         per_row = cols // 4
         assert NLOAD % per_row == 0 and per_row & (per_row - 1) == 0
         self.gen, self.rows, self.sbo = gen, rows, sbo
@@ -150,7 +165,7 @@ class _TileCopy:
         for t in range(min(self.P, self.iters)):
             rt = gen.register(".u32")
             gen.emit(f"add.u32 {rt}, {r0}, {self.rstep * t};")
-            off = _mn32_offset(gen, rt, cn, sbo)
+            off = _mn32_offset(gen, rt, cn, sbo, lbo)
             gen.emit(f"add.u32 {off}, {off}, {base};")
             self.bases.append(off)
         self.pv = None
@@ -171,11 +186,19 @@ class _TileCopy:
             gen.emit(f"{pred}ld.global.nc.v4.f32 {{{', '.join(regs)}}}, [{a}+{i * self.gstep}];")
         return out
 
-    def store(self, regs, hi, lo):
+    def store(self, regs, hi, lo, shift=None):
+        """Split and store the loaded tile; ``shift`` (a register, bytes) selects the buffer."""
         gen = self.gen
         step = (self.rstep * self.P // 4) * self.sbo
+        bases = self.bases
+        if shift is not None:
+            bases = []
+            for b in self.bases:
+                r = gen.register(".u32")
+                gen.emit(f"add.u32 {r}, {b}, {shift};")
+                bases.append(r)
         for i, four in enumerate(regs):
-            b = self.bases[i % self.P]
+            b = bases[i % self.P]
             imm = (i // self.P) * step
             his, los = tf32_split_pairs(gen, four)
             pred = f"@{self.pv} " if (self.pv and i == self.iters - 1) else ""
@@ -285,6 +308,18 @@ def _tree(gen, op, regs):
     return level[0]
 
 
+def _block_before(gen, J, k):
+    """J - k in a fresh register (a block index k blocks back)."""
+    r = gen.register(".u32")
+    gen.emit(f"sub.u32 {r}, {J}, {k};")
+    return r
+
+
+def _wait_pair(wait, gen, B, first, block, **kw):
+    """Wait until barrier pair ``first`` has completed the phase of block ``block``."""
+    wait(_pair_barrier(gen, B, first, block), _parity(gen, block, shift=1), **kw)
+
+
 def _pair_barrier(gen, B, first, counter):
     """Address of barrier ``first`` + (counter & 1) (the two barriers are adjacent)."""
     r = gen.register(".u32")
@@ -305,24 +340,35 @@ def lower_attention(gen, kernel, plan):
     # P in tensor memory when it fits (D = 64: Q 128 + S 128 + O 64 + P hi/lo 128 columns):
     # the softmax writes it with tcgen05.st and P*V reads A from TMEM; otherwise (D = 128)
     # P goes through shared memory in the K-major SWIZZLE_128B layout
-    c["P_TMEM"] = 3 * D + 4 * BKV <= TMEM_COLS
+    c["P_TMEM"] = _p_in_tmem(D, BKV)
     c.update(PTHI=3 * D + 2 * BKV, PTLO=3 * D + 3 * BKV)
-    # dynamic shared memory (1024-aligned): kt hi/lo, v hi/lo, P hi/lo
+    # dynamic shared memory (1024-aligned): NBUF x (kt hi, kt lo), NBUF x (v hi, v lo), P hi/lo
+    NBUF = tile_buffers(D, int(kernel.launch.get("smem_bytes", 0) or 0))
     K_BYTES, V_BYTES, P_BYTES = D * BKV * 4, BKV * D * 4, TQ * BKV * 4
-    c.update(KHI=0, KLO=K_BYTES, VHI=2 * K_BYTES, VLO=2 * K_BYTES + V_BYTES,
-             PHI=2 * K_BYTES + 2 * V_BYTES, PLO=2 * K_BYTES + 2 * V_BYTES + P_BYTES)
+    VBASE = NBUF * 2 * K_BYTES
+    PBASE = VBASE + NBUF * 2 * V_BYTES
+    c.update(NBUF=NBUF, KHI=0, KLO=K_BYTES, KSTEP=2 * K_BYTES, VHI=VBASE, VLO=VBASE + V_BYTES,
+             VSTEP=2 * V_BYTES, PHI=PBASE, PLO=PBASE + P_BYTES)
     NEED = c["PHI"] if c["P_TMEM"] else c["PLO"] + P_BYTES
-    c.update(SBO_K=16 * BKV, SBO_V=16 * D)     # 4-row K groups of the kt and v tiles
+    # kt [K = D rows, N = keys] and v [K = keys, N = D] tiles, MN-major SWIZZLE_128B_BASE32B:
+    # each 32-wide column strip is a contiguous run of 128-byte rows (4-row groups 512 B apart,
+    # strips rows x 128 B apart)
+    c.update(SBO_K=512, LBO_K=D * 128, SBO_V=512, LBO_V=BKV * 128)
     gen.maxntid = THREADS
 
     gen.module_decl(".global .align 4 .u32 emmy_error;")
     gen.module_decl(".extern .shared .align 1024 .b8 emmy_dsmem[];")
+    # Barrier pairs are indexed by the block's parity, their phase by (block >> 1) & 1.
     # SGO[b]: S of the next block using TMEM S buffer b may start (its kt tile is stored, 96
     #         loader arrivals, and the softmax has read the buffer's previous S, 128 arrivals);
-    # SFULL[b]: that S has completed (tcgen05.commit) -- also frees the kt tile for the loader;
-    # PVGO: P*V of the block may start (P written, 128; v tile stored, 96);
-    # PVDONE: it has completed -- frees P and the v tile, and O may be read or rescaled.
-    names = ["SGO0", "SGO1", "SFULL0", "SFULL1", "PVGO", "PVDONE", "QREADY", "DRAIN"]
+    # SFULL[b]: that S has completed (tcgen05.commit) -- also frees its kt tile for the loader;
+    # PVGO: P of the block is written (128 softmax arrivals; P has one buffer);
+    # VFULL[b]: the block's v tile is stored (96 loader arrivals; the loader may be a block
+    #           ahead with two tile buffers, so it has barriers of its own);
+    # PVDONE[b]: P*V of the block has completed -- frees P and its v tile, and O may be read
+    #            or rescaled.
+    names = ["SGO0", "SGO1", "SFULL0", "SFULL1", "PVGO", "VFULL0", "VFULL1", "PVDONE0",
+             "PVDONE1", "QREADY", "DRAIN"]
     gen.shared("emmy_bar", ".b64", length=len(names), align=8)
     gen.shared("emmy_tmem_slot", ".b32", length=1, align=4)
 
@@ -364,7 +410,8 @@ def lower_attention(gen, kernel, plan):
     gen.emit(f"setp.eq.u32 {p_t0}, {tid}, 0;")
     L_noinit = gen.new_label("noinit")
     gen.emit(f"@!{p_t0} bra {L_noinit};")
-    counts = {"SGO0": NLOAD + 128, "SGO1": NLOAD + 128, "PVGO": NLOAD + 128, "QREADY": 128}
+    counts = {"SGO0": NLOAD + 128, "SGO1": NLOAD + 128, "PVGO": 128, "VFULL0": NLOAD,
+              "VFULL1": NLOAD, "QREADY": 128}
     for n in names:
         gen.emit(f"mbarrier.init.shared::cta.b64 [{B[n]}], {counts.get(n, 1)};")
     gen.emit("fence.mbarrier_init.release.cluster;")
@@ -569,7 +616,7 @@ def _softmax_role(gen, ptr, plan, tid, warp, tmem, base, B, wait, cta, ncta, c):
             L_norescale = gen.new_label("noresc")
             if first is not False:
                 gen.emit(f"@{first} bra.uni {L_norescale};")
-            wait(B["PVDONE"], _parity(gen, J, minus=1))
+            _wait_pair(wait, gen, B, "PVDONE0", _block_before(gen, J, 1))
             gen.emit("tcgen05.fence::after_thread_sync;")
             for cb in range(D // 16):
                 regs = gen.registers(".f32", 16)
@@ -603,7 +650,7 @@ def _softmax_role(gen, ptr, plan, tid, warp, tmem, base, B, wait, cta, ncta, c):
         pz = gen.register(".pred")
         gen.emit(f"setp.eq.u32 {pz}, {J}, 0;")
         gen.emit(f"@{pz} bra.uni {L_nopw};")
-        wait(B["PVDONE"], _parity(gen, J, minus=1))
+        _wait_pair(wait, gen, B, "PVDONE0", _block_before(gen, J, 1))
         gen.label(L_nopw)
         if c["P_TMEM"]:
             for cb in range(BKV // 32):
@@ -632,7 +679,7 @@ def _softmax_role(gen, ptr, plan, tid, warp, tmem, base, B, wait, cta, ncta, c):
         close_j()
     block(NB == 1, True)
     # epilogue: O / l once the last P*V has landed
-    wait(B["PVDONE"], _parity(gen, J, minus=1))
+    _wait_pair(wait, gen, B, "PVDONE0", _block_before(gen, J, 1))
     gen.emit("tcgen05.fence::after_thread_sync;")
     inv = gen.register(".f32")
     gen.emit(f"rcp.rn.f32 {inv}, {lsum};")
@@ -668,13 +715,25 @@ def _mma_role(gen, tmem, base, B, wait, cta, ncta, lane, c):
     hi_k, hi_v, hi_p = (gen.register(".u32") for _ in range(3))
     gen.emit(f"mov.u32 {hi_k}, {(c['SBO_K'] >> 4) | (1 << 14) | (1 << 29)};")
     gen.emit(f"mov.u32 {hi_v}, {(c['SBO_V'] >> 4) | (1 << 14) | (1 << 29)};")
+    lbo_k, lbo_v = (c["LBO_K"] >> 4) << 16, (c["LBO_V"] >> 4) << 16
+
+    def tile_shift(block, step):
+        """Shared-memory descriptor offset (16-byte units) of block ``block``'s tile buffer."""
+        if c["NBUF"] == 1:
+            return None
+        r = gen.register(".u32")
+        gen.emit(f"and.b32 {r}, {block}, 1;")
+        gen.emit(f"mul.lo.u32 {r}, {r}, {step >> 4};")
+        return r
     gen.emit(f"mov.u32 {hi_p}, {(1024 >> 4) | (1 << 14) | (2 << 29)};")
     sb4 = gen.register(".u32")
     gen.emit(f"shr.u32 {sb4}, {base}, 4;")
 
-    def desc(lo_const, hi_reg):
+    def desc(lo_const, hi_reg, shift=None):
         lo = gen.register(".u32")
         gen.emit(f"add.u32 {lo}, {sb4}, {lo_const};")
+        if shift is not None:
+            gen.emit(f"add.u32 {lo}, {lo}, {shift};")
         d = gen.register(".b64")
         gen.emit(f"mov.b64 {d}, {{{lo}, {hi_reg}}};")
         return d
@@ -694,13 +753,14 @@ def _mma_role(gen, tmem, base, B, wait, cta, ncta, lane, c):
         gen.emit(f"and.b32 {dcol}, {J}, 1;")
         gen.emit(f"mad.lo.u32 {dcol}, {dcol}, {BKV}, {tmem};")
         gen.emit(f"add.u32 {dcol}, {dcol}, {c['S0']};")
+        kshift = tile_shift(J, c["KSTEP"])
         for ks in range(D // 8):
             a_hi, a_lo = gen.register(".u32"), gen.register(".u32")
             gen.emit(f"add.u32 {a_hi}, {tmem}, {c['QHI'] + ks * 8};")
             gen.emit(f"add.u32 {a_lo}, {tmem}, {c['QLO'] + ks * 8};")
             kadv = (2 * c["SBO_K"] * ks) >> 4
-            b_hi = desc(((c["KHI"] >> 4) + kadv) | (32 << 16), hi_k)
-            b_lo = desc(((c["KLO"] >> 4) + kadv) | (32 << 16), hi_k)
+            b_hi = desc(((c["KHI"] >> 4) + kadv) | lbo_k, hi_k, kshift)
+            b_lo = desc(((c["KLO"] >> 4) + kadv) | lbo_k, hi_k, kshift)
             acc = p_false if ks == 0 else p_true
             for a, b, en in ((a_hi, b_hi, acc), (a_hi, b_lo, p_true), (a_lo, b_hi, p_true)):
                 gen.emit(f"@{p_el} tcgen05.mma.cta_group::1.kind::tf32 [{dcol}], [{a}], {b}, "
@@ -710,7 +770,9 @@ def _mma_role(gen, tmem, base, B, wait, cta, ncta, lane, c):
     def issue_pv(Jp, first):
         """O (+)= P_Jp V_Jp; ``first``: True/False or a predicate true on an item's block 0."""
         wait(B["PVGO"], _parity(gen, Jp))
+        _wait_pair(wait, gen, B, "VFULL0", Jp)
         gen.emit("tcgen05.fence::after_thread_sync;")
+        vshift = tile_shift(Jp, c["VSTEP"])
         if first is True:
             acc0 = p_false
         elif first is False:
@@ -731,13 +793,13 @@ def _mma_role(gen, tmem, base, B, wait, cta, ncta, lane, c):
                 a_hi = desc(((c["PHI"] + patom * TQ * 128 + pin) >> 4) | (1 << 16), hi_p)
                 a_lo = desc(((c["PLO"] + patom * TQ * 128 + pin) >> 4) | (1 << 16), hi_p)
             vadv = (2 * c["SBO_V"] * ks) >> 4
-            b_hi = desc(((c["VHI"] >> 4) + vadv) | (32 << 16), hi_v)
-            b_lo = desc(((c["VLO"] >> 4) + vadv) | (32 << 16), hi_v)
+            b_hi = desc(((c["VHI"] >> 4) + vadv) | lbo_v, hi_v, vshift)
+            b_lo = desc(((c["VLO"] >> 4) + vadv) | lbo_v, hi_v, vshift)
             acc = acc0 if ks == 0 else p_true
             for a, b, en in ((a_hi, b_hi, acc), (a_hi, b_lo, p_true), (a_lo, b_hi, p_true)):
                 gen.emit(f"@{p_el} tcgen05.mma.cta_group::1.kind::tf32 [{dcol}], {a}, {b}, "
                          f"{r_io}, {en};")
-        commit(B["PVDONE"])
+        commit(_pair_barrier(gen, B, "PVDONE0", Jp))
 
     item, close_item = _item_loop(gen, cta, ncta, c["NITEMS"], "mitem")
     wait(B["QREADY"], _parity(gen, icount))
@@ -767,16 +829,19 @@ def _mma_role(gen, tmem, base, B, wait, cta, ncta, lane, c):
 def _load_role(gen, ptr, plan, tid, base, B, wait, cta, ncta, c):
     """kt and v tiles of each key block -> hi/lo MN-major tiles in shared memory.
 
-    The tensor core runs S_j, PV_(j-1), S_(j+1), PV_j, ... with one kt and one v buffer, so
-    kt_(j+1) can be written while PV_(j-1) runs (S_j has released the kt buffer) and v_j
-    while S_(j+1) runs (PV_(j-1) has released the v buffer): the kt tiles are kept one
-    block ahead of the v tiles. The global loads of each tile are issued a step before its
-    buffer wait, so L2 latency overlaps the tensor-core work."""
-    D, NB, NQB, BKV = c["D"], c["NB"], c["NQB"], c["BKV"]
+    The tensor core runs S_j, PV_(j-1), S_(j+1), PV_j, ... The kt tile of block j + 1 is
+    stored a block ahead of the v tile of block j. With NBUF tile buffers, the kt tile of block
+    X goes to buffer X % NBUF once S_(X - NBUF) has released it, and the v tile of block X
+    once PV_(X - NBUF) has: with two buffers a tile is stored while the tensor core still
+    reads the other one. The global loads of each tile are issued a step before its buffer
+    wait, so L2 latency overlaps the tensor-core work."""
+    D, NB, NQB, BKV, NBUF = c["D"], c["NB"], c["NQB"], c["BKV"], c["NBUF"]
     lt = gen.register(".u32")
     gen.emit(f"sub.u32 {lt}, {tid}, 160;")
-    ktc = _TileCopy(gen, lt, rows=D, cols=BKV, row_stride=c["Skv"], sbo=c["SBO_K"], base=base)
-    vc = _TileCopy(gen, lt, rows=BKV, cols=D, row_stride=D, sbo=c["SBO_V"], base=base)
+    ktc = _TileCopy(gen, lt, rows=D, cols=BKV, row_stride=c["Skv"], sbo=c["SBO_K"], base=base,
+                    lbo=c["LBO_K"])
+    vc = _TileCopy(gen, lt, rows=BKV, cols=D, row_stride=D, sbo=c["SBO_V"], base=base,
+                   lbo=c["LBO_V"])
     J = gen.register(".u32")
     gen.emit(f"mov.u32 {J}, 0;")
     item, close_item = _item_loop(gen, cta, ncta, c["NITEMS"], "litem")
@@ -789,36 +854,41 @@ def _load_role(gen, ptr, plan, tid, base, B, wait, cta, ncta, c):
     kregs = ktc.load(kt_t)
     vregs = vc.load(v_t)
 
-    def s_done(block):
-        """Wait until S of global block ``block`` (a register) has completed."""
-        wait(_pair_barrier(gen, B, "SFULL0", block), _parity(gen, block, shift=1))
+    def buf_shift(block, step):
+        if NBUF == 1:
+            return None
+        r = gen.register(".u32")
+        gen.emit(f"and.b32 {r}, {block}, 1;")
+        gen.emit(f"mul.lo.u32 {r}, {r}, {step};")
+        return r
+
+    def after(block, k, first, hint):
+        """Wait for barrier pair ``first`` of block ``block - k`` unless block < k."""
+        p = gen.register(".pred")
+        gen.emit(f"setp.lt.u32 {p}, {block}, {k};")
+        L = gen.new_label(hint)
+        gen.emit(f"@{p} bra.uni {L};")
+        _wait_pair(wait, gen, B, first, _block_before(gen, block, k))
+        gen.label(L)
 
     def put_k(block):
-        """kt tile (in kregs) of global block ``block`` -> buffer; counts toward SGO."""
-        ktc.store(kregs, c["KHI"], c["KLO"])
+        """kt tile (in kregs) of global block ``block`` -> its buffer, once S of the block
+        NBUF earlier has released it; counts toward SGO."""
+        after(block, NBUF, "SFULL0", "kfree")
+        ktc.store(kregs, c["KHI"], c["KLO"], buf_shift(block, c["KSTEP"]))
         gen.emit("fence.proxy.async.shared::cta;")
         gen.emit(f"mbarrier.arrive.shared::cta.b64 _, [{_pair_barrier(gen, B, 'SGO0', block)}];")
 
-    # kt_0 of this item: the buffer was last read by the previous block's S (global J - 1)
-    pz = gen.register(".pred")
-    gen.emit(f"setp.eq.u32 {pz}, {J}, 0;")
-    L_k0 = gen.new_label("k0nowait")
-    gen.emit(f"@{pz} bra.uni {L_k0};")
-    jm = gen.register(".u32")
-    gen.emit(f"sub.u32 {jm}, {J}, 1;")
-    s_done(jm)
-    gen.label(L_k0)
-    put_k(J)
+    put_k(J)                                        # kt of this item's first block
     if NB > 1:
         gen.emit(f"add.s64 {kt_t}, {kt_t}, {BKV * 4};")
         ktc.load(kt_t, into=kregs)
     j, close_j = _counted_loop(gen, NB, "lblk")
-    # kt_(j+1) once S_j has completed
+    # kt of block J + 1
     pk = gen.register(".pred")
     gen.emit(f"setp.lt.u32 {pk}, {j}, {NB - 1};")
     L_nok = gen.new_label("nonextk")
     gen.emit(f"@!{pk} bra.uni {L_nok};")
-    s_done(J)
     jn = gen.register(".u32")
     gen.emit(f"add.u32 {jn}, {J}, 1;")
     put_k(jn)
@@ -830,16 +900,11 @@ def _load_role(gen, ptr, plan, tid, base, B, wait, cta, ncta, c):
     ktc.load(kt_t, into=kregs)
     gen.label(L_nok2)
     gen.label(L_nok)
-    # v_j once P*V of the previous block has completed
-    pz2 = gen.register(".pred")
-    gen.emit(f"setp.eq.u32 {pz2}, {J}, 0;")
-    L_v = gen.new_label("novwait")
-    gen.emit(f"@{pz2} bra.uni {L_v};")
-    wait(B["PVDONE"], _parity(gen, J, minus=1))
-    gen.label(L_v)
-    vc.store(vregs, c["VHI"], c["VLO"])
+    # v of block J, once P*V of the block NBUF earlier has released its buffer
+    after(J, NBUF, "PVDONE0", "vfree")
+    vc.store(vregs, c["VHI"], c["VLO"], buf_shift(J, c["VSTEP"]))
     gen.emit("fence.proxy.async.shared::cta;")
-    gen.emit(f"mbarrier.arrive.shared::cta.b64 _, [{B['PVGO']}];")
+    gen.emit(f"mbarrier.arrive.shared::cta.b64 _, [{_pair_barrier(gen, B, 'VFULL0', J)}];")
     L_nov = gen.new_label("nonextv")
     gen.emit(f"@!{pk} bra.uni {L_nov};")
     gen.emit(f"add.s64 {v_t}, {v_t}, {BKV * D * 4};")
