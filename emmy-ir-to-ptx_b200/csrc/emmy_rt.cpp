@@ -72,6 +72,13 @@ struct Driver {
   EMMY_FN(StreamDestroy, CUresult, (CUstream))
   EMMY_FN(StreamQuery, CUresult, (CUstream))
   EMMY_FN(GetErrorString, CUresult, (CUresult, const char **))
+  // optional: without them modules keep their register-staged loads
+  EMMY_FN(TensorMapEncodeTiled, CUresult,
+          (CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+           const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+           CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill))
+  EMMY_FN(StreamIsCapturing, CUresult, (CUstream, CUstreamCaptureStatus *))
+  EMMY_FN(CtxSynchronize, CUresult, (void))
 #undef EMMY_FN
 };
 
@@ -129,6 +136,10 @@ void load_driver() {
   bind(h, d.StreamDestroy, "cuStreamDestroy_v2", m);
   bind(h, d.StreamQuery, "cuStreamQuery", m);
   bind(h, d.GetErrorString, "cuGetErrorString", m);
+  std::string optional;
+  bind(h, d.TensorMapEncodeTiled, "cuTensorMapEncodeTiled", optional);
+  bind(h, d.StreamIsCapturing, "cuStreamIsCapturing", optional);
+  bind(h, d.CtxSynchronize, "cuCtxSynchronize", optional);
   if (!m.empty()) {
     g_drv.why = "libcuda.so.1 lacks:" + m;
     return;
@@ -173,11 +184,140 @@ __attribute__((visibility("hidden"))) void emmy_rt_internal_set_error(const char
   snprintf(g_err, sizeof(g_err), "%s", msg ? msg : "");
 }
 
+// Tensor maps a module asks the runtime to write before its launches. The compiler declares
+// emmy_tmap_desc (what to encode), emmy_tmap (the maps) and emmy_tmap_key (the pointer each
+// map was encoded for); the kernel compares the keys with its own parameters and takes its
+// TMA path only when they all match, so a stale or missing map costs speed, never results.
+// A map is rewritten only when a launch's pointers differ from the keys, and only after every
+// earlier launch of the module has finished (so no running kernel reads a map being written);
+// the copies go on the launch stream in front of the kernel, maps before keys.
+constexpr uint32_t kTmapMagic = 0x454D5401u;
+constexpr int kTmapWords = 24;
+constexpr int kTmapMax = 4;
+
+struct TensorMaps {
+  int n = 0;                      // maps the module declares (0: none)
+  uint32_t desc[kTmapWords * kTmapMax] = {};
+  CUdeviceptr maps = 0, keys = 0;
+  uint64_t key[kTmapMax] = {};    // host copy of the device keys
+  int enabled = 1;
+  int frozen = 0;                 // launched under stream capture: never rewritten again
+  uint64_t uploads = 0;
+  std::vector<std::pair<CUstream, CUevent>> launched;   // last launch per stream
+  alignas(64) CUtensorMap staged[kTmapMax];
+  uint64_t staged_keys[kTmapMax] = {};
+};
+
 struct emmy_module {
   CUmodule mod = nullptr;
   CUfunction fn = nullptr;
   int dyn_smem_set = 0;
+  TensorMaps tm;
 };
+
+namespace {
+
+// Reads the module's tensor-map table, if it has one. A table that is present but malformed
+// is an error (only this compiler writes it).
+int tmap_setup(emmy_module *m) {
+  CUdeviceptr p = 0;
+  size_t n = 0;
+  CUresult r = g_drv.ModuleGetGlobal(&p, &n, m->mod, "emmy_tmap_desc");
+  if (r == CUDA_ERROR_NOT_FOUND) return EMMY_RT_OK;
+  CU(r, "cuModuleGetGlobal(emmy_tmap_desc)");
+  uint32_t head[2] = {0, 0};
+  if (n < sizeof(head)) return fail(EMMY_RT_EINVAL, "tensor-map table too short");
+  CU(g_drv.MemcpyDtoH(head, p, sizeof(head)), "cuMemcpyDtoH");
+  int count = int(head[1]);
+  if (head[0] != kTmapMagic || count < 1 || count > kTmapMax ||
+      n < sizeof(head) + size_t(count) * kTmapWords * 4)
+    return fail(EMMY_RT_EINVAL, "malformed tensor-map table");
+  TensorMaps &t = m->tm;
+  CU(g_drv.MemcpyDtoH(t.desc, p + sizeof(head), size_t(count) * kTmapWords * 4),
+     "cuMemcpyDtoH");
+  size_t bm = 0, bk = 0;
+  CU(g_drv.ModuleGetGlobal(&t.maps, &bm, m->mod, "emmy_tmap"), "cuModuleGetGlobal(emmy_tmap)");
+  CU(g_drv.ModuleGetGlobal(&t.keys, &bk, m->mod, "emmy_tmap_key"),
+     "cuModuleGetGlobal(emmy_tmap_key)");
+  if (bm < size_t(count) * 128 || bk < size_t(count) * 8 || (t.maps & 63))
+    return fail(EMMY_RT_EINVAL, "tensor-map globals too small or misaligned");
+  for (int k = 0; k < count; ++k) {
+    uint32_t rank = t.desc[k * kTmapWords + 1];
+    if (rank < 1 || rank > 5) return fail(EMMY_RT_EINVAL, "tensor-map rank out of range");
+  }
+  t.n = g_drv.TensorMapEncodeTiled && g_drv.StreamIsCapturing && g_drv.CtxSynchronize ? count : 0;
+  return EMMY_RT_OK;
+}
+
+bool tmap_encode(const uint32_t *d, uint64_t ptr, CUtensorMap *out) {
+  cuuint32_t rank = d[1];
+  cuuint64_t dims[5], strides[4];
+  cuuint32_t box[5], estr[5];
+  for (int i = 0; i < 5; ++i) {
+    dims[i] = d[2 + i];
+    box[i] = d[15 + i];
+    estr[i] = 1;
+  }
+  for (int i = 0; i < 4; ++i)
+    strides[i] = cuuint64_t(d[7 + 2 * i]) | (cuuint64_t(d[8 + 2 * i]) << 32);
+  return g_drv.TensorMapEncodeTiled(out, CUtensorMapDataType(d[21]), rank,
+                                    reinterpret_cast<void *>(static_cast<uintptr_t>(ptr)), dims,
+                                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                    CUtensorMapSwizzle(d[20]), CUtensorMapL2promotion(d[22]),
+                                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Before a launch: bring the device maps in line with this launch's pointers when that is
+// safe. Sets *track when the launch is to be recorded for later updates.
+int tmap_prepare(emmy_module *m, const uint64_t *args, int nargs, CUstream s, bool *track) {
+  TensorMaps &t = m->tm;
+  *track = false;
+  if (!t.n || !t.enabled) return EMMY_RT_OK;
+  CUstreamCaptureStatus cap = CU_STREAM_CAPTURE_STATUS_NONE;
+  CU(g_drv.StreamIsCapturing(s, &cap), "cuStreamIsCapturing");
+  if (cap != CU_STREAM_CAPTURE_STATUS_NONE) {
+    t.frozen = 1;   // a graph may replay this launch at any time from now on
+    return EMMY_RT_OK;
+  }
+  *track = true;
+  uint64_t want[kTmapMax] = {};
+  bool same = true;
+  for (int k = 0; k < t.n; ++k) {
+    uint32_t idx = t.desc[k * kTmapWords];
+    if (int(idx) >= nargs) return EMMY_RT_OK;
+    want[k] = args[idx];
+    same = same && want[k] == t.key[k];
+  }
+  if (same || t.frozen) return EMMY_RT_OK;
+  for (int k = 0; k < t.n; ++k)
+    if (!tmap_encode(&t.desc[k * kTmapWords], want[k], &t.staged[k]))
+      return EMMY_RT_OK;   // e.g. a pointer that is not 16-byte aligned: no TMA for it
+  for (auto &e : t.launched) CU(g_drv.EventSynchronize(e.second), "cuEventSynchronize");
+  std::memcpy(t.staged_keys, want, sizeof(want));
+  CU(g_drv.MemcpyHtoDAsync(t.maps, t.staged, size_t(t.n) * 128, s), "cuMemcpyHtoDAsync");
+  CU(g_drv.MemcpyHtoDAsync(t.keys, t.staged_keys, size_t(t.n) * 8, s), "cuMemcpyHtoDAsync");
+  std::memcpy(t.key, want, sizeof(want));
+  ++t.uploads;
+  return EMMY_RT_OK;
+}
+
+// After a launch: remember it, per stream, so a later rewrite can wait for it.
+int tmap_track(emmy_module *m, CUstream s) {
+  TensorMaps &t = m->tm;
+  for (auto &e : t.launched)
+    if (e.first == s) return cu_check(g_drv.EventRecord(e.second, s), "cuEventRecord");
+  CUevent ev = nullptr;
+  CU(g_drv.EventCreate(&ev, CU_EVENT_DISABLE_TIMING), "cuEventCreate");
+  t.launched.emplace_back(s, ev);
+  return cu_check(g_drv.EventRecord(ev, s), "cuEventRecord");
+}
+
+void tmap_release(emmy_module *m) {
+  for (auto &e : m->tm.launched) g_drv.EventDestroy(e.second);
+  m->tm.launched.clear();
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -258,6 +398,12 @@ int emmy_rt_module_load(const char *ptx, const char *entry, emmy_module **out, c
   emmy_module *m = new emmy_module;
   m->mod = mod;
   m->fn = fn;
+  rc = tmap_setup(m);
+  if (rc) {
+    g_drv.ModuleUnload(mod);
+    delete m;
+    return rc;
+  }
   *out = m;
   return EMMY_RT_OK;
 }
@@ -266,6 +412,7 @@ int emmy_rt_module_unload(emmy_module *m) {
   if (!m) return EMMY_RT_OK;
   int rc = need_driver();
   if (rc) return rc;
+  tmap_release(m);
   CUresult r = g_drv.ModuleUnload(m->mod);
   delete m;
   return cu_check(r, "cuModuleUnload");
@@ -314,6 +461,26 @@ int emmy_rt_module_error_word(emmy_module *m, uint32_t *value, int clear) {
   return EMMY_RT_OK;
 }
 
+int emmy_rt_module_tensor_maps(emmy_module *m, int enable, int *nmaps, uint64_t *uploads) {
+  if (!m) return fail(EMMY_RT_EINVAL, "null module");
+  if (enable < -1 || enable > 1) return fail(EMMY_RT_EINVAL, "enable must be -1, 0 or 1");
+  int rc = ensure_context();
+  if (rc) return rc;
+  TensorMaps &t = m->tm;
+  if (enable == 0 && t.n && t.enabled) {
+    for (auto &e : t.launched) CU(g_drv.EventSynchronize(e.second), "cuEventSynchronize");
+    CU(g_drv.MemsetD8(t.keys, 0, size_t(t.n) * 8), "cuMemsetD8");
+    CU(g_drv.CtxSynchronize(), "cuCtxSynchronize");
+    std::memset(t.key, 0, sizeof(t.key));
+    t.enabled = 0;
+  } else if (enable == 1) {
+    t.enabled = 1;
+  }
+  if (nmaps) *nmaps = t.n;
+  if (uploads) *uploads = t.uploads;
+  return EMMY_RT_OK;
+}
+
 static int launch_raw(emmy_module *m, const uint32_t grid[3], const uint32_t block[3],
                       uint32_t smem_bytes, const uint64_t *args, int nargs, CUstream stream,
                       uint32_t flags = 0) {
@@ -323,6 +490,9 @@ static int launch_raw(emmy_module *m, const uint32_t grid[3], const uint32_t blo
        "cuFuncSetAttribute(MAX_DYNAMIC_SHARED_SIZE_BYTES)");
     m->dyn_smem_set = int(smem_bytes);
   }
+  bool track = false;
+  int trc = tmap_prepare(m, args, nargs, stream, &track);
+  if (trc) return trc;
   std::vector<uint64_t> vals(args, args + nargs);
   std::vector<void *> params(static_cast<size_t>(nargs));
   for (int i = 0; i < nargs; ++i) params[size_t(i)] = &vals[size_t(i)];
@@ -348,12 +518,12 @@ static int launch_raw(emmy_module *m, const uint32_t grid[3], const uint32_t blo
     cfg.numAttrs = 1;
     CU(g_drv.LaunchKernelEx(&cfg, m->fn, nargs ? params.data() : nullptr, nullptr),
        "cuLaunchKernelEx");
-    return EMMY_RT_OK;
+  } else {
+    CU(g_drv.LaunchKernel(m->fn, grid[0], grid[1], grid[2], block[0], block[1], block[2],
+                          smem_bytes, stream, nargs ? params.data() : nullptr, nullptr),
+       "cuLaunchKernel");
   }
-  CU(g_drv.LaunchKernel(m->fn, grid[0], grid[1], grid[2], block[0], block[1], block[2],
-                        smem_bytes, stream, nargs ? params.data() : nullptr, nullptr),
-     "cuLaunchKernel");
-  return EMMY_RT_OK;
+  return track ? tmap_track(m, stream) : EMMY_RT_OK;
 }
 
 int emmy_rt_launch(emmy_module *m, const uint32_t grid[3], const uint32_t block[3],

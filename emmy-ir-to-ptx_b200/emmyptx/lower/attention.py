@@ -24,9 +24,16 @@ Warp roles (256 threads):
   memory) into one of two S buffers and O += P_j V_j (both operands in shared
   memory); S runs one block ahead of P*V so the tensor core overlaps the
   softmax;
-* warps 5-7: load the kt and v tiles of a key block with 16-byte loads (the
-  next kt tile is in flight while the v tile waits for its buffer), split them
-  and store them MN-major in SWIZZLE_128B_BASE32B (the TF32 MN-major layout).
+* warps 5-7: fill the kt and v tiles of each key block, MN-major in
+  SWIZZLE_128B_BASE32B (the TF32 MN-major layout). When the runtime has written
+  tensor maps for the launch's kt and v pointers, warp 5 copies each raw tile
+  with ``cp.async.bulk.tensor`` (the raw f32 words serve as the hi operand: the
+  MMA reads their top 19 bits) and warps 6-7 write the lo tile from it; the MMA
+  warp issues the hi x hi and lo x hi products as soon as the copy lands and the
+  hi x lo products once the lo tile is written. Otherwise all three warps load
+  the tiles with 16-byte loads (the next kt tile in flight while the v tile
+  waits for its buffer), split them and store hi and lo. Both paths give the same
+  bits.
 
 Hand-offs use mbarriers (loads -> MMA, MMA commit -> softmax, softmax -> MMA);
 every wait is bounded and warp-uniform; on expiry it sets bit 3 of
@@ -38,6 +45,7 @@ from __future__ import annotations
 
 from math import gcd
 
+from . import tmap
 from .common import WAIT_LIMIT, pack2, tf32_split_pairs, unpack2
 
 TQ = 128
@@ -48,6 +56,7 @@ TQ = 128
 BKV_FOR_D = {64: 64, 128: 64}
 THREADS = 256
 NLOAD = 96                 # loader threads: warps 5-7
+NWORK = 64                 # TMA path: lo-tile workers, warps 6-7 (warp 5 issues the copies)
 RESCALE_BITS = "0f41000000"   # 8.0: raise the running maximum only past 2^8 of growth
 
 
@@ -367,17 +376,33 @@ def lower_attention(gen, kernel, plan):
     #           ahead with two tile buffers, so it has barriers of its own);
     # PVDONE[b]: P*V of the block has completed -- frees P and its v tile, and O may be read
     #            or rescaled.
+    # On the TMA path the producer lane arrives for all 96 loader threads on SGO / VFULL once
+    # it has issued a tile's copy, and
+    # KRAW[b] / VRAW[b]: the copy of a block's raw kt / v tile has landed (expect_tx);
+    # KLO[b] / VLO[b]: its lo tile is written (64 worker arrivals).
+    # The MMA warp issues the products that read only the raw tile (hi x hi, lo x hi) after
+    # KRAW / VRAW and the hi x lo products after KLO / VLO.
     names = ["SGO0", "SGO1", "SFULL0", "SFULL1", "PVGO", "VFULL0", "VFULL1", "PVDONE0",
-             "PVDONE1", "QREADY", "DRAIN"]
+             "PVDONE1", "QREADY", "DRAIN", "KRAW0", "KRAW1", "VRAW0", "VRAW1", "KLO0", "KLO1",
+             "VLO0", "VLO1"]
     gen.shared("emmy_bar", ".b64", length=len(names), align=8)
     gen.shared("emmy_tmem_slot", ".b32", length=1, align=4)
 
-    ptr = {}
+    # tensor maps of kt [G, D, Skv] and v [G, Skv, D] (innermost first), boxes of 32
+    # columns: one box fills one column strip of a tile buffer
+    tmap.declare(gen, [
+        tmap.record(kernel.arg_order.index(plan.kt), [plan.Skv, D, plan.G],
+                    [plan.Skv * 4, D * plan.Skv * 4], [32, D, 1]),
+        tmap.record(kernel.arg_order.index(plan.v), [D, plan.Skv, plan.G],
+                    [D * 4, plan.Skv * D * 4], [32, BKV, 1]),
+    ])
+
+    ptr, raw_ptr = {}, {}
     for name in kernel.arg_order:
         raw, g = gen.register(".u64"), gen.register(".u64")
         gen.emit(f"ld.param.u64 {raw}, [{gen.parameter(name)}];")
         gen.emit(f"cvta.to.global.u64 {g}, {raw};")
-        ptr[name] = g
+        ptr[name], raw_ptr[name] = g, raw
 
     tid, warp, lane = (gen.register(".u32") for _ in range(3))
     gen.emit(f"mov.u32 {tid}, %tid.x;")
@@ -411,7 +436,8 @@ def lower_attention(gen, kernel, plan):
     L_noinit = gen.new_label("noinit")
     gen.emit(f"@!{p_t0} bra {L_noinit};")
     counts = {"SGO0": NLOAD + 128, "SGO1": NLOAD + 128, "PVGO": 128, "VFULL0": NLOAD,
-              "VFULL1": NLOAD, "QREADY": 128}
+              "VFULL1": NLOAD, "QREADY": 128, "KLO0": NWORK, "KLO1": NWORK, "VLO0": NWORK,
+              "VLO1": NWORK}
     for n in names:
         gen.emit(f"mbarrier.init.shared::cta.b64 [{B[n]}], {counts.get(n, 1)};")
     gen.emit("fence.mbarrier_init.release.cluster;")
@@ -435,6 +461,8 @@ def lower_attention(gen, kernel, plan):
     gen.emit(f"mov.u32 {cta}, %ctaid.x;")
     gen.emit(f"mov.u32 {ncta}, %nctaid.x;")
 
+    # the TMA path when the runtime has written maps for exactly these kt and v pointers
+    p_tma = tmap.keys_match(gen, [raw_ptr[plan.kt], raw_ptr[plan.v]])
     L_exit = gen.new_label("exit")
     wait = _Wait(gen, L_exit)
     L_mma, L_load = gen.new_label("mma_role"), gen.new_label("load_role")
@@ -446,10 +474,10 @@ def lower_attention(gen, kernel, plan):
     _softmax_role(gen, ptr, plan, tid, warp, tmem, base, B, wait, cta, ncta, c)
     gen.emit(f"bra {L_exit};")
     gen.label(L_mma)
-    _mma_role(gen, tmem, base, B, wait, cta, ncta, lane, c)
+    _mma_role(gen, tmem, base, B, wait, cta, ncta, lane, c, p_tma)
     gen.emit(f"bra {L_exit};")
     gen.label(L_load)
-    _load_role(gen, ptr, plan, tid, base, B, wait, cta, ncta, c)
+    _load_role(gen, ptr, p_tma, plan, tid, base, B, wait, cta, ncta, c)
 
     gen.label(L_exit)
     L_nodrain = gen.new_label("nodrain")
@@ -698,7 +726,7 @@ def _softmax_role(gen, ptr, plan, tid, warp, tmem, base, B, wait, cta, ncta, c):
 
 # ------------------------------------------------------------------ MMA warp 4
 
-def _mma_role(gen, tmem, base, B, wait, cta, ncta, lane, c):
+def _mma_role(gen, tmem, base, B, wait, cta, ncta, lane, c, p_tma):
     BKV = c["BKV"]
     D, NB = c["D"], c["NB"]
     p_el, el = gen.register(".pred"), gen.register(".u32")
@@ -742,6 +770,14 @@ def _mma_role(gen, tmem, base, B, wait, cta, ncta, lane, c):
         gen.emit(f"@{p_el} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
                  f"[{bar_addr}];")
 
+    def tma_wait(first, block):
+        """On the TMA path only: wait for barrier pair ``first`` of block ``block``."""
+        L = gen.new_label("notma")
+        gen.emit(f"@!{p_tma} bra.uni {L};")
+        _wait_pair(wait, gen, B, first, block)
+        gen.emit("tcgen05.fence::after_thread_sync;")
+        gen.label(L)
+
     J, icount = gen.register(".u32"), gen.register(".u32")
     gen.emit(f"mov.u32 {J}, 0;")
     gen.emit(f"mov.u32 {icount}, 0;")
@@ -754,6 +790,8 @@ def _mma_role(gen, tmem, base, B, wait, cta, ncta, lane, c):
         gen.emit(f"mad.lo.u32 {dcol}, {dcol}, {BKV}, {tmem};")
         gen.emit(f"add.u32 {dcol}, {dcol}, {c['S0']};")
         kshift = tile_shift(J, c["KSTEP"])
+        tma_wait("KRAW0", J)
+        lo_products = []
         for ks in range(D // 8):
             a_hi, a_lo = gen.register(".u32"), gen.register(".u32")
             gen.emit(f"add.u32 {a_hi}, {tmem}, {c['QHI'] + ks * 8};")
@@ -762,9 +800,14 @@ def _mma_role(gen, tmem, base, B, wait, cta, ncta, lane, c):
             b_hi = desc(((c["KHI"] >> 4) + kadv) | lbo_k, hi_k, kshift)
             b_lo = desc(((c["KLO"] >> 4) + kadv) | lbo_k, hi_k, kshift)
             acc = p_false if ks == 0 else p_true
-            for a, b, en in ((a_hi, b_hi, acc), (a_hi, b_lo, p_true), (a_lo, b_hi, p_true)):
+            for a, b, en in ((a_hi, b_hi, acc), (a_lo, b_hi, p_true)):
                 gen.emit(f"@{p_el} tcgen05.mma.cta_group::1.kind::tf32 [{dcol}], [{a}], {b}, "
                          f"{r_is}, {en};")
+            lo_products.append((a_hi, b_lo))
+        tma_wait("KLO0", J)
+        for a, b in lo_products:
+            gen.emit(f"@{p_el} tcgen05.mma.cta_group::1.kind::tf32 [{dcol}], [{a}], {b}, "
+                     f"{r_is}, {p_true};")
         commit(_pair_barrier(gen, B, "SFULL0", J))
 
     def issue_pv(Jp, first):
@@ -782,6 +825,8 @@ def _mma_role(gen, tmem, base, B, wait, cta, ncta, lane, c):
             gen.emit(f"not.pred {acc0}, {first};")
         dcol = gen.register(".u32")
         gen.emit(f"add.u32 {dcol}, {tmem}, {c['O']};")
+        tma_wait("VRAW0", Jp)
+        lo_products = []
         for ks in range(BKV // 8):
             if c["P_TMEM"]:                  # A = P from tensor memory, 8 columns per step
                 a_hi, a_lo = gen.register(".u32"), gen.register(".u32")
@@ -796,9 +841,14 @@ def _mma_role(gen, tmem, base, B, wait, cta, ncta, lane, c):
             b_hi = desc(((c["VHI"] >> 4) + vadv) | lbo_v, hi_v, vshift)
             b_lo = desc(((c["VLO"] >> 4) + vadv) | lbo_v, hi_v, vshift)
             acc = acc0 if ks == 0 else p_true
-            for a, b, en in ((a_hi, b_hi, acc), (a_hi, b_lo, p_true), (a_lo, b_hi, p_true)):
+            for a, b, en in ((a_hi, b_hi, acc), (a_lo, b_hi, p_true)):
                 gen.emit(f"@{p_el} tcgen05.mma.cta_group::1.kind::tf32 [{dcol}], {a}, {b}, "
                          f"{r_io}, {en};")
+            lo_products.append((a_hi, b_lo))
+        tma_wait("VLO0", Jp)
+        for a, b in lo_products:
+            gen.emit(f"@{p_el} tcgen05.mma.cta_group::1.kind::tf32 [{dcol}], {a}, {b}, "
+                     f"{r_io}, {p_true};")
         commit(_pair_barrier(gen, B, "PVDONE0", Jp))
 
     item, close_item = _item_loop(gen, cta, ncta, c["NITEMS"], "mitem")
@@ -826,7 +876,40 @@ def _mma_role(gen, tmem, base, B, wait, cta, ncta, lane, c):
 
 # ------------------------------------------------------------------ loader warps 5-7
 
-def _load_role(gen, ptr, plan, tid, base, B, wait, cta, ncta, c):
+def _load_role(gen, ptr, p_tma, plan, tid, base, B, wait, cta, ncta, c):
+    """Warps 5-7: the TMA path when the runtime has written tensor maps for this launch's kt
+    and v pointers, else the register-staged path. Bit 0 of ``emmy_path`` records a CTA on
+    the TMA path, bit 1 one on the register path."""
+    L_tma, L_done = gen.new_label("ld_tma"), gen.new_label("ld_done")
+    gen.emit(f"@{p_tma} bra.uni {L_tma};")
+    _load_lsu(gen, ptr, plan, tid, base, B, wait, cta, ncta, c)
+    gen.emit(f"bra.uni {L_done};")
+    gen.label(L_tma)
+    _load_tma(gen, plan, tid, base, B, wait, cta, ncta, c)
+    gen.label(L_done)
+
+
+def _after(gen, wait, B, block, k, first, hint, **kw):
+    """Wait for barrier pair ``first`` of block ``block - k`` unless block < k."""
+    p = gen.register(".pred")
+    gen.emit(f"setp.lt.u32 {p}, {block}, {k};")
+    L = gen.new_label(hint)
+    gen.emit(f"@{p} bra.uni {L};")
+    _wait_pair(wait, gen, B, first, _block_before(gen, block, k), **kw)
+    gen.label(L)
+
+
+def _buf_shift(gen, c, block, step):
+    """Byte offset of block ``block``'s tile buffer (None with one buffer)."""
+    if c["NBUF"] == 1:
+        return None
+    r = gen.register(".u32")
+    gen.emit(f"and.b32 {r}, {block}, 1;")
+    gen.emit(f"mul.lo.u32 {r}, {r}, {step};")
+    return r
+
+
+def _load_lsu(gen, ptr, plan, tid, base, B, wait, cta, ncta, c):
     """kt and v tiles of each key block -> hi/lo MN-major tiles in shared memory.
 
     The tensor core runs S_j, PV_(j-1), S_(j+1), PV_j, ... The kt tile of block j + 1 is
@@ -838,6 +921,9 @@ def _load_role(gen, ptr, plan, tid, base, B, wait, cta, ncta, c):
     D, NB, NQB, BKV, NBUF = c["D"], c["NB"], c["NQB"], c["BKV"], c["NBUF"]
     lt = gen.register(".u32")
     gen.emit(f"sub.u32 {lt}, {tid}, 160;")
+    p_l0 = gen.register(".pred")
+    gen.emit(f"setp.eq.u32 {p_l0}, {lt}, 0;")
+    gen.emit(f"@{p_l0} red.global.or.b32 [emmy_path], 2;")
     ktc = _TileCopy(gen, lt, rows=D, cols=BKV, row_stride=c["Skv"], sbo=c["SBO_K"], base=base,
                     lbo=c["LBO_K"])
     vc = _TileCopy(gen, lt, rows=BKV, cols=D, row_stride=D, sbo=c["SBO_V"], base=base,
@@ -855,21 +941,10 @@ def _load_role(gen, ptr, plan, tid, base, B, wait, cta, ncta, c):
     vregs = vc.load(v_t)
 
     def buf_shift(block, step):
-        if NBUF == 1:
-            return None
-        r = gen.register(".u32")
-        gen.emit(f"and.b32 {r}, {block}, 1;")
-        gen.emit(f"mul.lo.u32 {r}, {r}, {step};")
-        return r
+        return _buf_shift(gen, c, block, step)
 
     def after(block, k, first, hint):
-        """Wait for barrier pair ``first`` of block ``block - k`` unless block < k."""
-        p = gen.register(".pred")
-        gen.emit(f"setp.lt.u32 {p}, {block}, {k};")
-        L = gen.new_label(hint)
-        gen.emit(f"@{p} bra.uni {L};")
-        _wait_pair(wait, gen, B, first, _block_before(gen, block, k))
-        gen.label(L)
+        _after(gen, wait, B, block, k, first, hint)
 
     def put_k(block):
         """kt tile (in kregs) of global block ``block`` -> its buffer, once S of the block
@@ -913,3 +988,173 @@ def _load_role(gen, ptr, plan, tid, base, B, wait, cta, ncta, c):
     gen.emit(f"add.u32 {J}, {J}, 1;")
     close_j()
     close_item()
+
+
+def _lo_pass(gen, wt, base, shift, src, dst, nbytes):
+    """Workers (64 threads): the lo part ``x - (x & 0xFFFFE000)`` of every f32 of the raw tile
+    at ``src`` into the same offsets at ``dst``. The raw tile stays in place as the hi operand:
+    a ``kind::tf32`` MMA reads only the top 19 bits of each f32 word, so the raw word and its
+    masked hi part give the same products. Thread ``wt`` owns the 16-byte chunks wt, wt + 64,
+    ...: each warp instruction covers 512 contiguous bytes (no bank conflicts), and the lo
+    tile has the hi tile's swizzled layout because the offsets are the same."""
+    cpt = nbytes // 16 // 64
+    assert cpt * 16 * 64 == nbytes
+    a = gen.register(".u32")
+    gen.emit(f"mad.lo.u32 {a}, {wt}, 16, {base};")
+    if shift is not None:
+        gen.emit(f"add.u32 {a}, {a}, {shift};")
+    for g0 in range(0, cpt, 8):
+        group = []
+        for i in range(g0, min(cpt, g0 + 8)):
+            regs = gen.registers(".b32", 4)
+            gen.emit(f"ld.shared.v4.b32 {{{', '.join(regs)}}}, [{a}+{src + i * 1024}];")
+            group.append((i, regs))
+        for i, regs in group:
+            _, los = tf32_split_pairs(gen, regs)
+            gen.emit(f"st.shared.v4.b32 [{a}+{dst + i * 1024}], {{{', '.join(los)}}};")
+
+
+def _load_tma(gen, plan, tid, base, B, wait, cta, ncta, c):
+    """TMA path. Warp 5 is the producer: once a tile buffer is free (S or P*V of the block
+    NBUF earlier has completed), its elected lane copies the block's raw kt or v tile into the
+    hi buffer with ``cp.async.bulk.tensor`` (one box per 32-column strip, completing on the
+    KRAW / VRAW barrier pair; no multicast, the maps cover this GPU's buffers only) and
+    arrives for all 96 loader threads on SGO / VFULL. Warps 6-7 wait for the copy, write the
+    lo tile and arrive on KLO / VLO. The tile order is the register path's: kt of block J + 1
+    before v of block J.
+    On an expired wait the producer waits (bounded) for the copies it has in flight before it
+    leaves, so none lands in shared memory after the CTA has exited."""
+    D, NB, NQB, BKV = c["D"], c["NB"], c["NQB"], c["BKV"]
+    K_BYTES, V_BYTES = D * BKV * 4, BKV * D * 4
+    lt = gen.register(".u32")
+    gen.emit(f"sub.u32 {lt}, {tid}, 160;")
+    p_prod = gen.register(".pred")
+    gen.emit(f"setp.lt.u32 {p_prod}, {lt}, 32;")
+    L_work, L_end = gen.new_label("tma_work"), gen.new_label("tma_end")
+    gen.emit(f"@!{p_prod} bra.uni {L_work};")
+
+    # ---- producer (warp 5)
+    p_el, el = gen.register(".pred"), gen.register(".u32")
+    gen.emit(f"elect.sync {el}|{p_el}, -1;")
+    tk, tv = tmap.map_address(gen, 0), tmap.map_address(gen, 1)
+    gen.emit(f"@{p_el} fence.proxy.tensormap::generic.acquire.gpu [{tk}], 128;")
+    gen.emit(f"@{p_el} fence.proxy.tensormap::generic.acquire.gpu [{tv}], 128;")
+    gen.emit(f"@{p_el} red.global.or.b32 [emmy_path], 1;")
+    L_drain = gen.new_label("tma_drain")
+    J, nk, nv, zero = (gen.register(".u32") for _ in range(4))
+    for r in (J, nk, nv, zero):
+        gen.emit(f"mov.u32 {r}, 0;")
+
+    def issue(X, key0, g, *, free, raw, go, step, hi, nbytes, lbo, strips, tm, coords):
+        _after(gen, wait, B, X, c["NBUF"], free, "pfree", exit_label=L_drain)
+        bar = _pair_barrier(gen, B, raw, X)
+        shift = _buf_shift(gen, c, X, step)
+        gen.emit(f"@{p_el} mbarrier.arrive.expect_tx.shared::cta.b64 _, [{bar}], {nbytes};")
+        for s in range(strips):
+            dst = gen.register(".u32")
+            gen.emit(f"add.u32 {dst}, {base}, {hi + s * lbo};")
+            if shift is not None:
+                gen.emit(f"add.u32 {dst}, {dst}, {shift};")
+            x, y = coords(s, key0)
+            gen.emit(f"@{p_el} cp.async.bulk.tensor.3d.shared::cluster.global.tile"
+                     f".mbarrier::complete_tx::bytes [{dst}], [{tm}, {{{x}, {y}, {g}}}], [{bar}];")
+        gen.emit(f"@{p_el} mbarrier.arrive.shared::cta.b64 _, "
+                 f"[{_pair_barrier(gen, B, go, X)}], {NLOAD};")
+
+    def strip_x(s):
+        if s == 0:
+            return zero
+        r = gen.register(".u32")
+        gen.emit(f"mov.u32 {r}, {32 * s};")
+        return r
+
+    def kcoords(s, key0):
+        if s == 0:
+            return key0, zero
+        x = gen.register(".u32")
+        gen.emit(f"add.u32 {x}, {key0}, {32 * s};")
+        return x, zero
+
+    def vcoords(s, key0):
+        return strip_x(s), key0
+
+    def issue_k(X, key0, g):
+        issue(X, key0, g, free="SFULL0", raw="KRAW0", go="SGO0", step=c["KSTEP"], hi=c["KHI"],
+              nbytes=K_BYTES, lbo=c["LBO_K"], strips=BKV // 32, tm=tk, coords=kcoords)
+        gen.emit(f"add.u32 {nk}, {X}, 1;")
+
+    def issue_v(X, key0, g):
+        issue(X, key0, g, free="PVDONE0", raw="VRAW0", go="VFULL0", step=c["VSTEP"],
+              hi=c["VHI"], nbytes=V_BYTES, lbo=c["LBO_V"], strips=D // 32, tm=tv,
+              coords=vcoords)
+        gen.emit(f"add.u32 {nv}, {X}, 1;")
+
+    item, close_item = _item_loop(gen, cta, ncta, c["NITEMS"], "pitem")
+    g = gen.register(".u32")
+    gen.emit(f"div.u32 {g}, {item}, {NQB};")
+    issue_k(J, zero, g)
+    j, close_j = _counted_loop(gen, NB, "pblk")
+    pk = gen.register(".pred")
+    gen.emit(f"setp.lt.u32 {pk}, {j}, {NB - 1};")
+    L_nok = gen.new_label("pnok")
+    gen.emit(f"@!{pk} bra.uni {L_nok};")
+    jn, kn = gen.register(".u32"), gen.register(".u32")
+    gen.emit(f"add.u32 {jn}, {J}, 1;")
+    gen.emit(f"mad.lo.u32 {kn}, {j}, {BKV}, {BKV};")
+    issue_k(jn, kn, g)
+    gen.label(L_nok)
+    kc = gen.register(".u32")
+    gen.emit(f"mul.lo.u32 {kc}, {j}, {BKV};")
+    issue_v(J, kc, g)
+    gen.emit(f"add.u32 {J}, {J}, 1;")
+    close_j()
+    close_item()
+    gen.label(L_drain)
+    for cnt, raw in ((nk, "KRAW0"), (nv, "VRAW0")):
+        for back in (1, 2):
+            p = gen.register(".pred")
+            gen.emit(f"setp.lt.u32 {p}, {cnt}, {back};")
+            L = gen.new_label("pdrain")
+            gen.emit(f"@{p} bra.uni {L};")
+            _wait_pair(wait, gen, B, raw, _block_before(gen, cnt, back), exit_label=None)
+            gen.label(L)
+    gen.emit(f"bra.uni {L_end};")
+
+    # ---- lo workers (warps 6-7)
+    gen.label(L_work)
+    wt = gen.register(".u32")
+    gen.emit(f"sub.u32 {wt}, {lt}, 32;")
+    W = gen.register(".u32")
+    gen.emit(f"mov.u32 {W}, 0;")
+
+    def lo(X, *, free, raw, go, step, hi, lo_, nbytes, hint):
+        _after(gen, wait, B, X, c["NBUF"], free, hint)
+        _wait_pair(wait, gen, B, raw, X)
+        _lo_pass(gen, wt, base, _buf_shift(gen, c, X, step), hi, lo_, nbytes)
+        gen.emit("fence.proxy.async.shared::cta;")
+        gen.emit(f"mbarrier.arrive.shared::cta.b64 _, [{_pair_barrier(gen, B, go, X)}];")
+
+    def lo_k(X):
+        lo(X, free="SFULL0", raw="KRAW0", go="KLO0", step=c["KSTEP"], hi=c["KHI"],
+           lo_=c["KLO"], nbytes=K_BYTES, hint="wkfree")
+
+    def lo_v(X):
+        lo(X, free="PVDONE0", raw="VRAW0", go="VLO0", step=c["VSTEP"], hi=c["VHI"],
+           lo_=c["VLO"], nbytes=V_BYTES, hint="wvfree")
+
+    witem, wclose_item = _item_loop(gen, cta, ncta, c["NITEMS"], "witem")
+    lo_k(W)
+    wj, wclose_j = _counted_loop(gen, NB, "wblk")
+    wpk = gen.register(".pred")
+    gen.emit(f"setp.lt.u32 {wpk}, {wj}, {NB - 1};")
+    L_wnok = gen.new_label("wnok")
+    gen.emit(f"@!{wpk} bra.uni {L_wnok};")
+    wn = gen.register(".u32")
+    gen.emit(f"add.u32 {wn}, {W}, 1;")
+    lo_k(wn)
+    gen.label(L_wnok)
+    lo_v(W)
+    gen.emit(f"add.u32 {W}, {W}, 1;")
+    wclose_j()
+    wclose_item()
+    gen.label(L_end)

@@ -72,6 +72,8 @@ def lib():
         "emmy_rt_module_error_word": ([c.c_void_p, c.POINTER(c.c_uint32), c.c_int], c.c_int),
         "emmy_rt_module_global": ([c.c_void_p, c.c_char_p, c.POINTER(c.c_uint64),
                                    c.POINTER(c.c_uint64)], c.c_int),
+        "emmy_rt_module_tensor_maps": ([c.c_void_p, c.c_int, c.POINTER(c.c_int),
+                                        c.POINTER(c.c_uint64)], c.c_int),
         "emmy_rt_launch": ([c.c_void_p, _U32x3, _U32x3, c.c_uint32, c.POINTER(c.c_uint64),
                             c.c_int, c.c_uint64], c.c_int),
         "emmy_rt_launch_ex": ([c.c_void_p, _U32x3, _U32x3, c.c_uint32, c.POINTER(c.c_uint64),
@@ -190,6 +192,29 @@ class Module:
         check(lib().emmy_rt_module_global(self.handle, name.encode(), ctypes.byref(p),
                                           ctypes.byref(n)))
         return p.value, n.value
+
+    def tensor_maps(self, enable=None) -> dict:
+        """Tensor maps the module declares and how often the runtime has written them;
+        ``enable=False`` stops writing them and clears the keys (the kernel then stages its
+        tiles through registers), ``enable=True`` resumes."""
+        n, up = ctypes.c_int(), ctypes.c_uint64()
+        mode = -1 if enable is None else int(bool(enable))
+        check(lib().emmy_rt_module_tensor_maps(self.handle, mode, ctypes.byref(n),
+                                               ctypes.byref(up)))
+        return {"maps": n.value, "uploads": up.value}
+
+    def path_word(self, clear=False) -> int:
+        """``emmy_path`` of a module with tensor maps (bit 0: a CTA loaded tiles by TMA,
+        bit 1: one staged them through registers); 0 for other modules."""
+        try:
+            p, _ = self.global_symbol("emmy_path")
+        except RuntimeErrorEmmy:
+            return 0
+        v = np.zeros(1, np.uint32)
+        check(lib().emmy_rt_memcpy_dtoh(v.ctypes.data, p, 4))
+        if clear:
+            check(lib().emmy_rt_memset_zero(p, 4))
+        return int(v[0])
 
     def launch(self, grid, block, smem, ptrs, stream=0, overlap=False):
         """Launch on ``stream``. ``overlap=True`` lets the grid start while the previous

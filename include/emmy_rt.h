@@ -90,6 +90,24 @@ int emmy_rt_module_error_word(emmy_module *m, uint32_t *value, int clear);
 /* Device address and size of a module-scope .global symbol. */
 int emmy_rt_module_global(emmy_module *m, const char *name, uint64_t *dptr, uint64_t *bytes);
 
+/* Tensor maps (no counterpart in the reference: its PTX ABI passes pointers only). A kernel
+ * that can load tiles with TMA (the attention template) declares a table `emmy_tmap_desc` of
+ * the maps it wants: per map the parameter index, rank, dims, byte strides, box, swizzle,
+ * data type and L2 promotion. Before a launch whose pointers differ from the ones the maps
+ * were last written for, every launch function of this library encodes them
+ * (cuTensorMapEncodeTiled) and copies them with their keys (the pointers) into the module's
+ * globals on the launch stream, after waiting for the module's earlier launches. The kernel
+ * uses TMA only when every key equals its own parameter and otherwise stages tiles through
+ * registers, so results never depend on the maps; a runner that does not write them (the
+ * reference's) gets the register path. Launches under stream capture never write maps, and
+ * after one the module's maps are frozen. Pointers TMA cannot take (not 16-byte aligned)
+ * leave the maps as they are.
+ * enable: 1 = write maps (the default), 0 = stop writing them and clear the keys (later
+ * launches take the register path; waits for the module's launches and the context), -1 =
+ * query only. nmaps: maps the module declares (0: none, or a driver without
+ * cuTensorMapEncodeTiled); uploads: map writes so far. */
+int emmy_rt_module_tensor_maps(emmy_module *m, int enable, int *nmaps, uint64_t *uploads);
+
 /* Launch with device-pointer arguments in arg_order (each a .u64 param).
  * Dynamic shared memory above 48 KiB is enabled on the function first, as
  * the runner does for meta.json smem_bytes (reference PROVENANCE.md). */
