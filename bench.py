@@ -672,6 +672,11 @@ def measure_config(name, args, peaks, l2, flush, *, device=0, compile_repeats=5,
                       flush_ptr=flush.ptr if do_flush else 0,
                       flush_bytes=flush.nbytes if do_flush else 0)
         entry["error_word"] = mod.error_word()
+        maps = mod.tensor_maps()
+        if maps["maps"]:
+            # which tile loads the timed launches used: bit 0 TMA, bit 1 registers
+            word = mod.path_word()
+            entry["tile_loads"] = {1: "tma", 2: "registers"}.get(word, f"mixed {word:#x}")
     finally:
         mod.close()
         for b in bufs:
