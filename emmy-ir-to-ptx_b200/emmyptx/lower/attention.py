@@ -28,9 +28,10 @@ Warp roles (256 threads):
   SWIZZLE_128B_BASE32B (the TF32 MN-major layout). When the runtime has written
   tensor maps for the launch's kt and v pointers, warp 5 copies each raw tile
   with ``cp.async.bulk.tensor`` (the raw f32 words serve as the hi operand: the
-  MMA reads their top 19 bits) and warps 6-7 write the lo tile from it; the MMA
-  warp issues the hi x hi and lo x hi products as soon as the copy lands and the
-  hi x lo products once the lo tile is written. Otherwise all three warps load
+  MMA reads their top 19 bits) and warps 6-7 write the lo tile from it; with one
+  buffer per tile (D = 128) the MMA warp issues the products that read only the
+  raw tile (hi x hi, lo x hi) as soon as the copy lands and the hi x lo products
+  once the lo tile is written. Otherwise all three warps load
   the tiles with 16-byte loads (the next kt tile in flight while the v tile
   waits for its buffer), split them and store hi and lo. Both paths give the same
   bits.
@@ -353,6 +354,8 @@ def lower_attention(gen, kernel, plan):
     c.update(PTHI=3 * D + 2 * BKV, PTLO=3 * D + 3 * BKV)
     # dynamic shared memory (1024-aligned): NBUF x (kt hi, kt lo), NBUF x (v hi, v lo), P hi/lo
     NBUF = tile_buffers(D, int(kernel.launch.get("smem_bytes", 0) or 0))
+    # one buffer per tile: split each product around the lo pass (see the barriers below)
+    c["SPLIT"] = NBUF == 1
     K_BYTES, V_BYTES, P_BYTES = D * BKV * 4, BKV * D * 4, TQ * BKV * 4
     VBASE = NBUF * 2 * K_BYTES
     PBASE = VBASE + NBUF * 2 * V_BYTES
@@ -368,23 +371,26 @@ def lower_attention(gen, kernel, plan):
     gen.module_decl(".global .align 4 .u32 emmy_error;")
     gen.module_decl(".extern .shared .align 1024 .b8 emmy_dsmem[];")
     # Barrier pairs are indexed by the block's parity, their phase by (block >> 1) & 1.
+    # Every wait costs the MMA warp (which sets the pace when the tiles come by TMA) well over
+    # a hundred cycles even when the phase has long completed, so each product waits on one
+    # barrier that gathers all it needs:
     # SGO[b]: S of the next block using TMEM S buffer b may start (its kt tile is stored, 96
     #         loader arrivals, and the softmax has read the buffer's previous S, 128 arrivals);
     # SFULL[b]: that S has completed (tcgen05.commit) -- also frees its kt tile for the loader;
-    # PVGO: P of the block is written (128 softmax arrivals; P has one buffer);
-    # VFULL[b]: the block's v tile is stored (96 loader arrivals; the loader may be a block
-    #           ahead with two tile buffers, so it has barriers of its own);
+    # PVGO[b]: P*V of the block may start (P written, 128 softmax arrivals; its v tile stored,
+    #          96 loader arrivals -- the loader may be a block ahead with two tile buffers);
     # PVDONE[b]: P*V of the block has completed -- frees P and its v tile, and O may be read
     #            or rescaled.
-    # On the TMA path the producer lane arrives for all 96 loader threads on SGO / VFULL once
-    # it has issued a tile's copy, and
-    # KRAW[b] / VRAW[b]: the copy of a block's raw kt / v tile has landed (expect_tx);
-    # KLO[b] / VLO[b]: its lo tile is written (64 worker arrivals).
-    # The MMA warp issues the products that read only the raw tile (hi x hi, lo x hi) after
-    # KRAW / VRAW and the hi x lo products after KLO / VLO.
-    names = ["SGO0", "SGO1", "SFULL0", "SFULL1", "PVGO", "VFULL0", "VFULL1", "PVDONE0",
-             "PVDONE1", "QREADY", "DRAIN", "KRAW0", "KRAW1", "VRAW0", "VRAW1", "KLO0", "KLO1",
-             "VLO0", "VLO1"]
+    # On the TMA path the producer lane arrives for its warp once it has issued a tile's copy,
+    # and KRAW[b] / VRAW[b] complete when the raw kt / v tile has landed (expect_tx); the
+    # workers arrive on SGO / PVGO once the lo tile is written. With one buffer per tile
+    # (D = 128) the copies are on the critical path: the producer then arrives for all 96 on
+    # SGO / PVGO, the MMA warp issues the products that read only the raw tile (hi x hi,
+    # lo x hi) after KRAW / VRAW and the hi x lo products after KLO[b] / VLO[b] (64 worker
+    # arrivals once the lo tile is written).
+    names = ["SGO0", "SGO1", "SFULL0", "SFULL1", "PVGO0", "PVGO1", "PVDONE0", "PVDONE1",
+             "QREADY", "DRAIN", "KRAW0", "KRAW1", "VRAW0", "VRAW1", "KLO0", "KLO1", "VLO0",
+             "VLO1"]
     gen.shared("emmy_bar", ".b64", length=len(names), align=8)
     gen.shared("emmy_tmem_slot", ".b32", length=1, align=4)
 
@@ -435,9 +441,9 @@ def lower_attention(gen, kernel, plan):
     gen.emit(f"setp.eq.u32 {p_t0}, {tid}, 0;")
     L_noinit = gen.new_label("noinit")
     gen.emit(f"@!{p_t0} bra {L_noinit};")
-    counts = {"SGO0": NLOAD + 128, "SGO1": NLOAD + 128, "PVGO": 128, "VFULL0": NLOAD,
-              "VFULL1": NLOAD, "QREADY": 128, "KLO0": NWORK, "KLO1": NWORK, "VLO0": NWORK,
-              "VLO1": NWORK}
+    counts = {"SGO0": NLOAD + 128, "SGO1": NLOAD + 128, "PVGO0": NLOAD + 128,
+              "PVGO1": NLOAD + 128, "QREADY": 128, "KLO0": NWORK, "KLO1": NWORK,
+              "VLO0": NWORK, "VLO1": NWORK}
     for n in names:
         gen.emit(f"mbarrier.init.shared::cta.b64 [{B[n]}], {counts.get(n, 1)};")
     gen.emit("fence.mbarrier_init.release.cluster;")
@@ -696,7 +702,7 @@ def _softmax_role(gen, ptr, plan, tid, warp, tmem, base, B, wait, cta, ncta, c):
                              f"{{{', '.join(regs)}}};")
             gen.emit("fence.proxy.async.shared::cta;")
         gen.emit("tcgen05.fence::before_thread_sync;")
-        gen.emit(f"mbarrier.arrive.shared::cta.b64 _, [{B['PVGO']}];")
+        gen.emit(f"mbarrier.arrive.shared::cta.b64 _, [{_pair_barrier(gen, B, 'PVGO0', J)}];")
         gen.emit(f"add.u32 {J}, {J}, 1;")
 
     if NB > 1:
@@ -790,7 +796,8 @@ def _mma_role(gen, tmem, base, B, wait, cta, ncta, lane, c, p_tma):
         gen.emit(f"mad.lo.u32 {dcol}, {dcol}, {BKV}, {tmem};")
         gen.emit(f"add.u32 {dcol}, {dcol}, {c['S0']};")
         kshift = tile_shift(J, c["KSTEP"])
-        tma_wait("KRAW0", J)
+        if c["SPLIT"]:
+            tma_wait("KRAW0", J)
         lo_products = []
         for ks in range(D // 8):
             a_hi, a_lo = gen.register(".u32"), gen.register(".u32")
@@ -804,7 +811,8 @@ def _mma_role(gen, tmem, base, B, wait, cta, ncta, lane, c, p_tma):
                 gen.emit(f"@{p_el} tcgen05.mma.cta_group::1.kind::tf32 [{dcol}], [{a}], {b}, "
                          f"{r_is}, {en};")
             lo_products.append((a_hi, b_lo))
-        tma_wait("KLO0", J)
+        if c["SPLIT"]:
+            tma_wait("KLO0", J)
         for a, b in lo_products:
             gen.emit(f"@{p_el} tcgen05.mma.cta_group::1.kind::tf32 [{dcol}], [{a}], {b}, "
                      f"{r_is}, {p_true};")
@@ -812,8 +820,7 @@ def _mma_role(gen, tmem, base, B, wait, cta, ncta, lane, c, p_tma):
 
     def issue_pv(Jp, first):
         """O (+)= P_Jp V_Jp; ``first``: True/False or a predicate true on an item's block 0."""
-        wait(B["PVGO"], _parity(gen, Jp))
-        _wait_pair(wait, gen, B, "VFULL0", Jp)
+        _wait_pair(wait, gen, B, "PVGO0", Jp)
         gen.emit("tcgen05.fence::after_thread_sync;")
         vshift = tile_shift(Jp, c["VSTEP"])
         if first is True:
@@ -825,7 +832,8 @@ def _mma_role(gen, tmem, base, B, wait, cta, ncta, lane, c, p_tma):
             gen.emit(f"not.pred {acc0}, {first};")
         dcol = gen.register(".u32")
         gen.emit(f"add.u32 {dcol}, {tmem}, {c['O']};")
-        tma_wait("VRAW0", Jp)
+        if c["SPLIT"]:
+            tma_wait("VRAW0", Jp)
         lo_products = []
         for ks in range(BKV // 8):
             if c["P_TMEM"]:                  # A = P from tensor memory, 8 columns per step
@@ -845,7 +853,8 @@ def _mma_role(gen, tmem, base, B, wait, cta, ncta, lane, c, p_tma):
                 gen.emit(f"@{p_el} tcgen05.mma.cta_group::1.kind::tf32 [{dcol}], {a}, {b}, "
                          f"{r_io}, {en};")
             lo_products.append((a_hi, b_lo))
-        tma_wait("VLO0", Jp)
+        if c["SPLIT"]:
+            tma_wait("VLO0", Jp)
         for a, b in lo_products:
             gen.emit(f"@{p_el} tcgen05.mma.cta_group::1.kind::tf32 [{dcol}], {a}, {b}, "
                      f"{r_io}, {p_true};")
@@ -979,7 +988,7 @@ def _load_lsu(gen, ptr, plan, tid, base, B, wait, cta, ncta, c):
     after(J, NBUF, "PVDONE0", "vfree")
     vc.store(vregs, c["VHI"], c["VLO"], buf_shift(J, c["VSTEP"]))
     gen.emit("fence.proxy.async.shared::cta;")
-    gen.emit(f"mbarrier.arrive.shared::cta.b64 _, [{_pair_barrier(gen, B, 'VFULL0', J)}];")
+    gen.emit(f"mbarrier.arrive.shared::cta.b64 _, [{_pair_barrier(gen, B, 'PVGO0', J)}];")
     L_nov = gen.new_label("nonextv")
     gen.emit(f"@!{pk} bra.uni {L_nov};")
     gen.emit(f"add.s64 {v_t}, {v_t}, {BKV * D * 4};")
@@ -1019,9 +1028,10 @@ def _load_tma(gen, plan, tid, base, B, wait, cta, ncta, c):
     NBUF earlier has completed), its elected lane copies the block's raw kt or v tile into the
     hi buffer with ``cp.async.bulk.tensor`` (one box per 32-column strip, completing on the
     KRAW / VRAW barrier pair; no multicast, the maps cover this GPU's buffers only) and
-    arrives for all 96 loader threads on SGO / VFULL. Warps 6-7 wait for the copy, write the
-    lo tile and arrive on KLO / VLO. The tile order is the register path's: kt of block J + 1
-    before v of block J.
+    arrives for its warp on SGO / PVGO (for all 96 loader threads when the products are split
+    around the lo pass, D = 128). Warps 6-7 wait for the copy, write the lo tile and arrive on
+    SGO / PVGO (KLO / VLO when split). The tile order is the register path's: kt of block
+    J + 1 before v of block J.
     On an expired wait the producer waits (bounded) for the copies it has in flight before it
     leaves, so none lands in shared memory after the CTA has exited."""
     D, NB, NQB, BKV = c["D"], c["NB"], c["NQB"], c["BKV"]
@@ -1045,7 +1055,7 @@ def _load_tma(gen, plan, tid, base, B, wait, cta, ncta, c):
     for r in (J, nk, nv, zero):
         gen.emit(f"mov.u32 {r}, 0;")
 
-    def issue(X, key0, g, *, free, raw, go, step, hi, nbytes, lbo, strips, tm, coords):
+    def issue(X, key0, g, *, free, raw, go, step, hi, nbytes, lbo, strips, tm, coords, share):
         _after(gen, wait, B, X, c["NBUF"], free, "pfree", exit_label=L_drain)
         bar = _pair_barrier(gen, B, raw, X)
         shift = _buf_shift(gen, c, X, step)
@@ -1059,7 +1069,7 @@ def _load_tma(gen, plan, tid, base, B, wait, cta, ncta, c):
             gen.emit(f"@{p_el} cp.async.bulk.tensor.3d.shared::cluster.global.tile"
                      f".mbarrier::complete_tx::bytes [{dst}], [{tm}, {{{x}, {y}, {g}}}], [{bar}];")
         gen.emit(f"@{p_el} mbarrier.arrive.shared::cta.b64 _, "
-                 f"[{_pair_barrier(gen, B, go, X)}], {NLOAD};")
+                 f"[{_pair_barrier(gen, B, go, X)}], {share};")
 
     def strip_x(s):
         if s == 0:
@@ -1080,13 +1090,14 @@ def _load_tma(gen, plan, tid, base, B, wait, cta, ncta, c):
 
     def issue_k(X, key0, g):
         issue(X, key0, g, free="SFULL0", raw="KRAW0", go="SGO0", step=c["KSTEP"], hi=c["KHI"],
-              nbytes=K_BYTES, lbo=c["LBO_K"], strips=BKV // 32, tm=tk, coords=kcoords)
+              nbytes=K_BYTES, lbo=c["LBO_K"], strips=BKV // 32, tm=tk, coords=kcoords,
+              share=NLOAD if c["SPLIT"] else NLOAD - NWORK)
         gen.emit(f"add.u32 {nk}, {X}, 1;")
 
     def issue_v(X, key0, g):
-        issue(X, key0, g, free="PVDONE0", raw="VRAW0", go="VFULL0", step=c["VSTEP"],
+        issue(X, key0, g, free="PVDONE0", raw="VRAW0", go="PVGO0", step=c["VSTEP"],
               hi=c["VHI"], nbytes=V_BYTES, lbo=c["LBO_V"], strips=D // 32, tm=tv,
-              coords=vcoords)
+              coords=vcoords, share=NLOAD if c["SPLIT"] else NLOAD - NWORK)
         gen.emit(f"add.u32 {nv}, {X}, 1;")
 
     item, close_item = _item_loop(gen, cta, ncta, c["NITEMS"], "pitem")
@@ -1135,11 +1146,13 @@ def _load_tma(gen, plan, tid, base, B, wait, cta, ncta, c):
         gen.emit(f"mbarrier.arrive.shared::cta.b64 _, [{_pair_barrier(gen, B, go, X)}];")
 
     def lo_k(X):
-        lo(X, free="SFULL0", raw="KRAW0", go="KLO0", step=c["KSTEP"], hi=c["KHI"],
+        lo(X, free="SFULL0", raw="KRAW0", go="KLO0" if c["SPLIT"] else "SGO0",
+           step=c["KSTEP"], hi=c["KHI"],
            lo_=c["KLO"], nbytes=K_BYTES, hint="wkfree")
 
     def lo_v(X):
-        lo(X, free="PVDONE0", raw="VRAW0", go="VLO0", step=c["VSTEP"], hi=c["VHI"],
+        lo(X, free="PVDONE0", raw="VRAW0", go="VLO0" if c["SPLIT"] else "PVGO0",
+           step=c["VSTEP"], hi=c["VHI"],
            lo_=c["VLO"], nbytes=V_BYTES, hint="wvfree")
 
     witem, wclose_item = _item_loop(gen, cta, ncta, c["NITEMS"], "witem")
