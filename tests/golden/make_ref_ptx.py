@@ -7,7 +7,8 @@ that runs them needs no checkout):
     python tests/golden/make_ref_ptx.py <reference checkout>/compile.py
 
 emmy-ml is not installable offline, so the reference runs against the stand-in package in
-``emmy_stub`` (``Graph.from_dict`` backed by this project's decoder). Outputs go to
+``emmy_stub``, whose ``Graph.from_dict`` has a decoder of its own (``ast`` over Emmy's repr
+text; nothing from this project is on the reference's path). Outputs go to
 ``ref_ptx/<name>.ptx`` with ``ref_ptx/MANIFEST.json`` recording, per PTX, its source (a fixture
 folder, or a workload constructor call and the SHA-256 of the IR + meta it produced), so a
 test can tell when a workload generator drifted from the IR the PTX was made from.
@@ -60,7 +61,7 @@ def make_variant(name):
 
 
 def _run_reference(compile_py, ir_path):
-    env = dict(os.environ, PYTHONPATH=os.pathsep.join([str(HERE / "emmy_stub"), str(PKG)]))
+    env = dict(os.environ, PYTHONPATH=str(HERE / "emmy_stub"))
     r = subprocess.run([sys.executable, str(compile_py), str(ir_path)], capture_output=True,
                        text=True, env=env, cwd=tempfile.gettempdir(), timeout=600)
     if r.returncode != 0:
