@@ -66,6 +66,7 @@ struct Driver {
   EMMY_FN(EventCreate, CUresult, (CUevent *, unsigned int))
   EMMY_FN(EventRecord, CUresult, (CUevent, CUstream))
   EMMY_FN(EventSynchronize, CUresult, (CUevent))
+  EMMY_FN(EventQuery, CUresult, (CUevent))
   EMMY_FN(EventElapsedTime, CUresult, (float *, CUevent, CUevent))
   EMMY_FN(EventDestroy, CUresult, (CUevent))
   EMMY_FN(StreamCreate, CUresult, (CUstream *, unsigned int))
@@ -130,6 +131,7 @@ void load_driver() {
   bind(h, d.EventCreate, "cuEventCreate", m);
   bind(h, d.EventRecord, "cuEventRecord", m);
   bind(h, d.EventSynchronize, "cuEventSynchronize", m);
+  bind(h, d.EventQuery, "cuEventQuery", m);
   bind(h, d.EventElapsedTime, "cuEventElapsedTime", m);
   bind(h, d.EventDestroy, "cuEventDestroy_v2", m);
   bind(h, d.StreamCreate, "cuStreamCreate", m);
@@ -301,11 +303,22 @@ int tmap_prepare(emmy_module *m, const uint64_t *args, int nargs, CUstream s, bo
   return EMMY_RT_OK;
 }
 
-// After a launch: remember it, per stream, so a later rewrite can wait for it.
+// After a launch: remember it, per stream, so a later rewrite can wait for it. Entries whose
+// launch has finished are dropped first (a host that makes a stream per call, as emmy_rt_run
+// does, would otherwise grow the list without bound).
 int tmap_track(emmy_module *m, CUstream s) {
   TensorMaps &t = m->tm;
   for (auto &e : t.launched)
     if (e.first == s) return cu_check(g_drv.EventRecord(e.second, s), "cuEventRecord");
+  for (size_t i = 0; i < t.launched.size();) {
+    if (g_drv.EventQuery(t.launched[i].second) == CUDA_SUCCESS) {
+      g_drv.EventDestroy(t.launched[i].second);
+      t.launched[i] = t.launched.back();
+      t.launched.pop_back();
+    } else {
+      ++i;
+    }
+  }
   CUevent ev = nullptr;
   CU(g_drv.EventCreate(&ev, CU_EVENT_DISABLE_TIMING), "cuEventCreate");
   t.launched.emplace_back(s, ev);

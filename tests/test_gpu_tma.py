@@ -157,3 +157,36 @@ def test_runner_path_takes_tma(gpu_runtime):
         assert mod.tensor_maps()["uploads"] == 1
     finally:
         mod.close()
+
+
+def test_runner_repeated_calls(gpu_runtime):
+    """Many ``emmy_rt_run`` calls on one module, each with buffers and a stream of its own:
+    every call writes the maps it needs (after the earlier calls' launches), takes the TMA path
+    and gives the same bits."""
+    from emmyptx import workloads
+    from emmyptx.emit import compile_payload
+    from oracle.expressions import kernel_inputs
+    payload, meta = workloads.attention(1, 2, 256, 64)
+    k = meta["kernels"][0]
+    ptx, _, _ = compile_payload(payload, meta)
+    mod = gpu_runtime.Module(ptx, k["entry"])
+    inputs = kernel_inputs(k)
+    results = []
+    try:
+        for _ in range(12):
+            host = []
+            for a in k["args"]:
+                if a.get("output"):
+                    out = np.zeros(a["shape"], np.float32)
+                    host.append((out, True, False))
+                else:
+                    host.append((np.ascontiguousarray(inputs[a["name"]]), False, False))
+            mod.path_word(clear=True)
+            mod.run(k["grid"], k["block"], k["smem_bytes"], host, warmup=0, iters=1)
+            assert mod.error_word() == 0 and mod.path_word() == TMA
+            results.append(out.copy())
+        assert mod.tensor_maps()["uploads"] >= 1
+        for r in results[1:]:
+            assert np.array_equal(r.view(np.uint32), results[0].view(np.uint32))
+    finally:
+        mod.close()
