@@ -208,6 +208,7 @@ struct TensorMaps {
   std::vector<std::pair<CUstream, CUevent>> launched;   // last launch per stream
   alignas(64) CUtensorMap staged[kTmapMax];
   uint64_t staged_keys[kTmapMax] = {};
+  std::mutex lock;                // launches of one module from several host threads
 };
 
 struct emmy_module {
@@ -480,6 +481,7 @@ int emmy_rt_module_tensor_maps(emmy_module *m, int enable, int *nmaps, uint64_t 
   int rc = ensure_context();
   if (rc) return rc;
   TensorMaps &t = m->tm;
+  std::lock_guard<std::mutex> guard(t.lock);
   if (enable == 0 && t.n && t.enabled) {
     for (auto &e : t.launched) CU(g_drv.EventSynchronize(e.second), "cuEventSynchronize");
     CU(g_drv.MemsetD8(t.keys, 0, size_t(t.n) * 8), "cuMemsetD8");
@@ -504,6 +506,10 @@ static int launch_raw(emmy_module *m, const uint32_t grid[3], const uint32_t blo
     m->dyn_smem_set = int(smem_bytes);
   }
   bool track = false;
+  // a module with tensor maps: its keys, maps and launch records change together with the
+  // launch that needs them
+  std::unique_lock<std::mutex> guard;
+  if (m->tm.n) guard = std::unique_lock<std::mutex>(m->tm.lock);
   int trc = tmap_prepare(m, args, nargs, stream, &track);
   if (trc) return trc;
   std::vector<uint64_t> vals(args, args + nargs);
