@@ -685,9 +685,8 @@ def measure_config(name, args, peaks, l2, flush, *, device=0, compile_repeats=5,
     entry.update({"us_median": round(us, 3), "us_min": round(min(ms) * 1e3, 3),
                   "launches": args.steps, "l2_flush": do_flush,
                   "compile_ms": round(cms, 2)})
-    if template == "pointwise" and "griddepcontrol.launch_dependents" in ptx:
-        ov = _overlapped_pointwise(ptx, k, inputs, footprint, l2, device,
-                                   max(4 * args.steps, 50))
+    if "griddepcontrol.launch_dependents" in ptx:
+        ov = _overlapped(ptx, k, inputs, footprint, l2, device, max(4 * args.steps, 50))
         ov["frac"] = round(ov["gbs"] / peaks["hbm_gbs"], 4)
         entry["overlapped"] = ov
     if proc_ms is not None:
@@ -713,16 +712,18 @@ def measure_config(name, args, peaks, l2, flush, *, device=0, compile_repeats=5,
     return entry
 
 
-def _overlapped_pointwise(ptx, k, inputs, footprint, l2, device, launches):
-    """Back-to-back launches of a pointwise kernel with programmatic stream serialization
-    (``EMMY_RT_LAUNCH_OVERLAP``): each launch may be scheduled while the previous one runs and
-    waits for it (``griddepcontrol.wait``) before touching memory. The launches cycle over
-    enough copies of the buffers to cover twice L2, so every launch reads its inputs from HBM.
-    Time per launch = the event-timed region over the launches."""
+def _overlapped(ptx, k, inputs, footprint, l2, device, launches):
+    """Back-to-back launches of a kernel that takes overlapped launches (pointwise, rows, full
+    sums) with programmatic stream serialization (``EMMY_RT_LAUNCH_OVERLAP``): each launch may
+    be scheduled while the previous one runs and orders its memory accesses after it
+    (``griddepcontrol.wait``). The launches cycle over enough copies of the buffers to cover
+    twice L2, so every launch reads its inputs from HBM. Time per launch = the event-timed
+    region over the launches."""
     import numpy as np
     import torch
     from emmyptx import runtime
     sets = max(2, -(-2 * l2 // footprint))
+    smem = k.get("smem_bytes", 0)
     mod = runtime.Module(ptx, k["entry"], device)
     bufs = []
     try:
@@ -740,12 +741,12 @@ def _overlapped_pointwise(ptx, k, inputs, footprint, l2, device, launches):
         stream = torch.cuda.current_stream(device)
         sh = stream.cuda_stream
         for i in range(2 * sets):                              # warm-up
-            mod.launch(k["grid"], k["block"], 0, ptr_sets[i % sets], sh, overlap=True)
+            mod.launch(k["grid"], k["block"], smem, ptr_sets[i % sets], sh, overlap=True)
         torch.cuda.synchronize(device)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for i in range(launches):
-            mod.launch(k["grid"], k["block"], 0, ptr_sets[i % sets], sh, overlap=True)
+            mod.launch(k["grid"], k["block"], smem, ptr_sets[i % sets], sh, overlap=True)
         e1.record(stream)
         torch.cuda.synchronize(device)
         us = e0.elapsed_time(e1) * 1e3 / launches

@@ -612,6 +612,13 @@ def _lower_rows(gen, kernel, plan, B):
     L, R = plan.length, plan.rows
     S = len(plan.states)
     ptrs = load_pointers(gen, list(kernel.arg_order))
+    # Launched with programmatic stream serialization (EMMY_RT_LAUNCH_OVERLAP; no effect under
+    # a plain launch), the next kernel on the stream may be scheduled once every CTA of this
+    # one has started, and this kernel touches global memory only after the previous one has
+    # finished: a chain of launches keeps its order and only the launch latency overlaps
+    # (the CTAs of the last wave are the last to trigger).
+    gen.emit("griddepcontrol.launch_dependents;")
+    gen.emit("griddepcontrol.wait;")
     uniforms = _hoist_uniforms(gen, plan, ptrs)
     NC = L // 4
     vec_ok = L % 4 == 0 and NC > 0

@@ -121,9 +121,11 @@ int emmy_rt_launch(emmy_module *m, const uint32_t grid[3], const uint32_t block[
  * mean kernels this compiler emits execute it once a thread has streamed 7/8
  * of its input (the next kernel then reads lines this one read more than an
  * L2's worth of bytes earlier, for inputs larger than L2), and run
- * griddepcontrol.wait before any global write; under a plain launch both
- * instructions do nothing. Only for back-to-back launches whose inputs the
- * previous kernel does not write.
+ * griddepcontrol.wait before any global write: only for back-to-back launches
+ * whose inputs the previous kernel does not write. The pointwise and row
+ * kernels execute both at entry, before any global access, so only the launch
+ * latency overlaps and a chain of launches (one's output the next one's
+ * input) keeps its order. Under a plain launch both instructions do nothing.
  * Not part of the reference runner's interface (an addition of this
  * library). */
 #define EMMY_RT_LAUNCH_OVERLAP 1u

@@ -98,3 +98,50 @@ def test_overlapped_pointwise_chain_stays_ordered():
     mod.close()
     for buf in ys + [bb]:
         buf.free()
+
+
+@pytest.mark.parametrize("op", ["softmax", "rmsnorm"])
+def test_overlapped_row_chain_stays_ordered(op):
+    """A chain of overlapped row-kernel launches, each reading the rows the previous one
+    wrote (12 launches over 2048 x 4096). The row kernels wait for their predecessor
+    (``griddepcontrol.wait``) before any global access, so the chain gives the bits of the
+    same launches made one after another without overlap."""
+    from emmyptx import runtime, workloads
+    from emmyptx.emit import compile_payload
+    from oracle.expressions import kernel_inputs
+    runtime.init(0)
+    payload, meta = workloads.row_op(op, rows=2048)
+    ptx, template, _ = compile_payload(payload, meta)
+    assert template == "rowreduce" and "griddepcontrol.wait" in ptx
+    k = meta["kernels"][0]
+    inputs = kernel_inputs(k)
+    out = next(a for a in k["args"] if a.get("output"))
+    x_name = next(a["name"] for a in k["args"]
+                  if not a.get("output") and a["shape"] == out["shape"])
+    others = [a["name"] for a in k["args"] if a["name"] not in (x_name, out["name"])]
+    steps = 12
+
+    def chain(overlap):
+        bufs = {n: runtime.DeviceBuffer.from_array(inputs[n]) for n in others}
+        ys = [runtime.DeviceBuffer.from_array(inputs[x_name])] + [
+            runtime.DeviceBuffer(inputs[x_name].nbytes) for _ in range(2)]
+        mod = runtime.Module(ptx, k["entry"])
+        src = 0
+        for i in range(steps):
+            dst = 1 + (i % 2)
+            where = {x_name: ys[src].ptr, out["name"]: ys[dst].ptr}
+            where.update({n: b.ptr for n, b in bufs.items()})
+            ptrs = [where[a["name"]] for a in k["args"]]
+            mod.launch(k["grid"], k["block"], k.get("smem_bytes", 0), ptrs, overlap=overlap)
+            src = dst
+        runtime.sync()
+        got = ys[src].download(np.zeros_like(inputs[x_name]))
+        assert mod.error_word() == 0
+        mod.close()
+        for b in list(bufs.values()) + ys:
+            b.free()
+        return got
+
+    plain, overlapped = chain(False), chain(True)
+    assert np.all(np.isfinite(plain))
+    assert np.array_equal(plain.view(np.uint32), overlapped.view(np.uint32))
