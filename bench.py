@@ -851,6 +851,7 @@ def run_suite_sharded(args, rank, world, local_rank):
                       flush_bytes=flush.nbytes if do_flush else 0)
         us = statistics.median(ms) * 1e3
         err = mod.error_word()
+        path = mod.path_word() if mod.tensor_maps()["maps"] else 0
         mod.close()
         for b in bufs:
             b.free()
@@ -876,8 +877,8 @@ def run_suite_sharded(args, rank, world, local_rank):
             e1.record()
             torch.cuda.synchronize()
             combine_us = e0.elapsed_time(e1) * 1e3 / 20
-        stats = torch.tensor([us + combine_us, us, combine_us, float(err)], device=dev,
-                             dtype=torch.float64)
+        stats = torch.tensor([us + combine_us, us, combine_us, float(err), float(path)],
+                             device=dev, dtype=torch.float64)
         every = [torch.zeros_like(stats) for _ in range(world)]
         dist.all_gather(every, stats)
         if rank != 0:
@@ -893,6 +894,9 @@ def run_suite_sharded(args, rank, world, local_rank):
                 "combine": (("emmy_rt_fold_f32" if fold is not None else "NCCL all-reduce")
                             if sh.combine else None),
                 "error_words": [int(v[3]) for v in every],
+                **({"tile_loads_per_rank": [{1: "tma", 2: "registers"}.get(int(v[4]), int(v[4]))
+                                            for v in every]} if any(int(v[4]) for v in every)
+                   else {}),
                 "shard_units": list(sh.units), "l2_flush": do_flush}
         shp = {a["name"]: a["shape"] for a in whole["args"]}
         if name.startswith("matmul") or name.startswith("attention"):
