@@ -54,7 +54,7 @@ TQ = 128
 # memory (Q hi/lo 256 + two S buffers 64 + O 128 + P hi/lo 64 = 512 columns) and cut the
 # shared-memory traffic per key by a third, ran 1.151 ms against 1.079-1.091 ms with 64-key
 # blocks: the per-block hand-offs, twice as many, cost more than the traffic saved
-BKV_FOR_D = {64: 64, 128: 64}
+BKV_FOR_D = {32: 64, 64: 64, 128: 64}
 THREADS = 256
 NLOAD = 96                 # loader threads: warps 5-7
 NWORK = 64                 # TMA path: lo-tile workers, warps 6-7 (warp 5 issues the copies)
@@ -74,9 +74,9 @@ def smem_bytes_needed(D, nbuf=1):
 
 
 def tile_buffers(D, smem):
-    """kt/v tile buffers: two at D = 64 when the launch's shared memory holds them (a tile can
-    then be stored while the tensor core still reads the other), else one."""
-    return 2 if D == 64 and smem >= smem_bytes_needed(D, 2) else 1
+    """kt/v tile buffers: two at D = 32 and 64 when the launch's shared memory holds them (a
+    tile can then be stored while the tensor core still reads the other), else one."""
+    return 2 if D <= 64 and smem >= smem_bytes_needed(D, 2) else 1
 
 
 def fits(plan, launch):
@@ -84,7 +84,7 @@ def fits(plan, launch):
     grid = list(launch.get("grid", [1, 1, 1]))
     if block != [THREADS, 1, 1] or grid[1:] != [1, 1]:
         return False
-    if plan.D not in (64, 128) or plan.Dv != plan.D:
+    if plan.D not in BKV_FOR_D or plan.Dv != plan.D:
         return False
     if plan.Sq % TQ or plan.Skv % BKV_FOR_D[plan.D]:
         return False

@@ -59,8 +59,9 @@ def test_attention_full_size(name, gpu_runtime):
 
 
 @pytest.mark.parametrize("shape", [(1, 2, 256, 128, None), (2, 1, 384, 64, None),
-                                   (1, 1, 512, 128, 0.25), (1, 2, 256, 64, 0.125)],
-                         ids=["d128", "d64", "d128-peaked", "d64-peaked"])
+                                   (1, 1, 512, 128, 0.25), (1, 2, 256, 64, 0.125),
+                                   (2, 4, 1024, 32, None), (1, 2, 256, 32, 0.125)],
+                         ids=["d128", "d64", "d128-peaked", "d64-peaked", "d32", "d32-peaked"])
 def test_attention_template_matches_fp64_and_walker(shape, gpu_runtime):
     """Small shapes: template and statement walker both within 1e-4 of fp64. A small divisor
     c makes the logits large, so the running maximum moves between key blocks and the

@@ -87,8 +87,11 @@ def test_tma_matches_register_path_full_size(name, gpu_runtime):
                                         ((2, 1, 384, 64, None), None),
                                         ((1, 1, 512, 128, 0.25), None),
                                         ((2, 2, 384, 128, None), 5),
-                                        ((1, 3, 128, 64, None), 1)],
-                         ids=["d128", "d64", "d128-peaked", "d128-grid5", "d64-grid1"])
+                                        ((1, 3, 128, 64, None), 1),
+                                        ((2, 2, 512, 32, None), None),
+                                        ((1, 3, 384, 32, 0.25), 2)],
+                         ids=["d128", "d64", "d128-peaked", "d128-grid5", "d64-grid1", "d32",
+                              "d32-peaked-grid2"])
 def test_tma_matches_register_path_small(shape, grid, gpu_runtime):
     """Small shapes (two to eight key blocks; several work items per CTA): bit-equal paths,
     and the TMA result within 1e-4 of fp64 (row-scaled, as the other attention checks)."""
