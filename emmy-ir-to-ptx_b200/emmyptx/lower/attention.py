@@ -54,7 +54,7 @@ TQ = 128
 # memory (Q hi/lo 256 + two S buffers 64 + O 128 + P hi/lo 64 = 512 columns) and cut the
 # shared-memory traffic per key by a third, ran 1.151 ms against 1.079-1.091 ms with 64-key
 # blocks: the per-block hand-offs, twice as many, cost more than the traffic saved
-BKV_FOR_D = {32: 64, 64: 64, 128: 64}
+BKV_FOR_D = {32: 64, 64: 64, 96: 64, 128: 64}
 THREADS = 256
 NLOAD = 96                 # loader threads: warps 5-7
 NWORK = 64                 # TMA path: lo-tile workers, warps 6-7 (warp 5 issues the copies)
@@ -157,15 +157,15 @@ class _TileCopy:
 
     def __init__(self, gen, lt, *, rows, cols, row_stride, sbo, base, lbo=512):
         per_row = cols // 4
-        assert NLOAD % per_row == 0 and per_row & (per_row - 1) == 0
+        assert NLOAD % per_row == 0
         self.gen, self.rows, self.sbo = gen, rows, sbo
         self.rstep = NLOAD // per_row
         self.iters = -(-(rows * per_row) // NLOAD)
         self.P = 4 // gcd(self.rstep, 4)
         self.gstep = self.rstep * row_stride * 4
         r0, cn = gen.register(".u32"), gen.register(".u32")
-        gen.emit(f"shr.u32 {r0}, {lt}, {per_row.bit_length() - 1};")
-        gen.emit(f"and.b32 {cn}, {lt}, {per_row - 1};")
+        gen.emit(f"div.u32 {r0}, {lt}, {per_row};")
+        gen.emit(f"rem.u32 {cn}, {lt}, {per_row};")
         e = gen.register(".u32")
         gen.emit(f"mul.lo.u32 {e}, {r0}, {row_stride};")
         gen.emit(f"mad.lo.u32 {e}, {cn}, 4, {e};")

@@ -89,16 +89,18 @@ def test_tma_matches_register_path_full_size(name, gpu_runtime):
                                         ((2, 2, 384, 128, None), 5),
                                         ((1, 3, 128, 64, None), 1),
                                         ((2, 2, 512, 32, None), None),
-                                        ((1, 3, 384, 32, 0.25), 2)],
+                                        ((1, 3, 384, 32, 0.25), 2),
+                                        ((2, 2, 512, 96, None), None),
+                                        ((1, 2, 384, 96, 0.25), 3)],
                          ids=["d128", "d64", "d128-peaked", "d128-grid5", "d64-grid1", "d32",
-                              "d32-peaked-grid2"])
+                              "d32-peaked-grid2", "d96", "d96-peaked-grid3"])
 def test_tma_matches_register_path_small(shape, grid, gpu_runtime):
     """Small shapes (two to eight key blocks; several work items per CTA): bit-equal paths,
     and the TMA result within 1e-4 of fp64 (row-scaled, as the other attention checks)."""
     from emmyptx import workloads
     from oracle.expressions import _attention
     B, H, S, D, c = shape
-    payload, meta = workloads.attention(B, H, S, D, scale=c)
+    payload, meta = workloads.attention(B, H, S, D, scale=c, stages=2 if D == 96 else 3)
     inputs, got_tma, got_regs = _both_paths(gpu_runtime, payload, meta, grid)
     assert np.array_equal(got_tma.view(np.uint32), got_regs.view(np.uint32))
     cc = float(inputs["div_c1"][0])
