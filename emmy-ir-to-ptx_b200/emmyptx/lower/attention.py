@@ -50,11 +50,12 @@ from . import tmap
 from .common import WAIT_LIMIT, pack2, tf32_split_pairs, unpack2
 
 TQ = 128
-# keys per block. Measured on B200 at D = 128: 32-key blocks, which let P live in tensor
-# memory (Q hi/lo 256 + two S buffers 64 + O 128 + P hi/lo 64 = 512 columns) and cut the
-# shared-memory traffic per key by a third, ran 1.151 ms against 1.079-1.091 ms with 64-key
-# blocks: the per-block hand-offs, twice as many, cost more than the traffic saved
-BKV_FOR_D = {32: 64, 64: 64, 96: 64, 128: 64}
+# keys per block. At D = 128, 32-key blocks let P live in tensor memory (Q hi/lo 256 + two S
+# buffers 64 + O 128 + P hi/lo 64 = 512 columns), which leaves the shared memory room for two
+# kt and two v buffers: with TMA-fed tiles and one barrier wait per product they ran 7.6 %
+# faster than 64-key blocks with one buffer each (interleaved on a B200); with register-staged
+# tiles and more hand-offs per block they had been slower (1.151 against 1.08 ms)
+BKV_FOR_D = {32: 64, 64: 64, 96: 64, 128: 32}
 THREADS = 256
 NLOAD = 96                 # loader threads: warps 5-7
 NWORK = 64                 # TMA path: lo-tile workers, warps 6-7 (warp 5 issues the copies)
@@ -76,7 +77,7 @@ def smem_bytes_needed(D, nbuf=1):
 def tile_buffers(D, smem):
     """kt/v tile buffers: two at D = 32 and 64 when the launch's shared memory holds them (a
     tile can then be stored while the tensor core still reads the other), else one."""
-    return 2 if D <= 64 and smem >= smem_bytes_needed(D, 2) else 1
+    return 2 if D != 96 and smem >= smem_bytes_needed(D, 2) else 1
 
 
 def fits(plan, launch):

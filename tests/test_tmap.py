@@ -6,6 +6,7 @@ import re
 import pytest
 
 from emmyptx.lower import tmap
+from emmyptx.lower.attention import BKV_FOR_D
 
 
 def _table(ptx):
@@ -46,12 +47,15 @@ def test_attention_declares_kt_and_v_maps(name, D):
     assert kt["param"] == order.index("kt") and v["param"] == order.index("v")
     assert kt["dims"] == [S, D, B * H] and kt["box"] == [32, D, 1]
     assert kt["strides"] == [S * 4, D * S * 4]
-    assert v["dims"] == [D, S, B * H] and v["box"] == [32, 64, 1]
+    bkv = BKV_FOR_D[D]
+    assert v["dims"] == [D, S, B * H] and v["box"] == [32, bkv, 1]
     assert v["strides"] == [D * 4, S * D * 4]
     for r in (kt, v):
         assert r["swizzle"] == tmap.SWIZZLE_128B_ATOM_32B and r["dtype"] == tmap.DTYPE_FLOAT32
         assert r["box"][0] * 4 == 128       # one box row = one 128-byte swizzle row
-    assert ptx.count("cp.async.bulk.tensor.3d") == 2 * (64 // 32) + D // 32
+    # kt copies at two sites (an item's first block, then each next one), a box per 32 keys;
+    # v: a box per 32 columns
+    assert ptx.count("cp.async.bulk.tensor.3d") == 2 * (bkv // 32) + D // 32
     assert "multicast" not in ptx
     assert "emmy_tmap_key" in ptx and "fence.proxy.tensormap::generic.acquire" in ptx
 
