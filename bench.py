@@ -47,6 +47,7 @@ N_REDUCE = 1 << 26
 PER_KERNEL = 10               # steps of the per-kernel (event-bracketed) timing pass
 HBM_NOMINAL_GBS = 8000.0      # B200 HBM3e nominal bandwidth, for context beside the measured peak
 RES_SLOTS = 4                 # result slots: an all-reduce may lag its step by 3 steps
+FOLD_SLOTS = 64               # result slots with the fold (a fold may lag its step by 63 steps)
 FALLBACK_HBM_GBS = 6650.0
 REF_STEP_S = 0.15             # reference arm: seconds of CPU work per step
 E2E_STEPS = 30                # e2e: timed steps (median)
@@ -256,34 +257,48 @@ def run_ours(args, rank, world, local_rank):
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
     x = torch.empty(N_REDUCE, device=dev, dtype=torch.float32).uniform_(-1, 1, generator=g)
     count = torch.tensor([float(N_REDUCE * world)], device=dev, dtype=torch.float32)
-    # RES_SLOTS result slots: step i writes slot i % RES_SLOTS, so the all-reduce of step i
-    # overlaps the kernels of the next RES_SLOTS - 1 steps; a slot's all-reduce is waited
-    # for (on the stream) before the slot is written again, and all are drained before the
-    # stop event
-    res = torch.zeros(RES_SLOTS, 2, device=dev, dtype=torch.float32)
-    stream = torch.cuda.current_stream(dev)
-    sh = stream.cuda_stream
-    grid3, block3 = k_s["grid"], k_s["block"]
-    p_sum = [[x.data_ptr(), res[i].data_ptr()] for i in range(RES_SLOTS)]
-    p_mean = [[x.data_ptr(), count.data_ptr(), res[i].data_ptr() + 4] for i in range(RES_SLOTS)]
-    assert [a["name"] for a in k_m["args"]] == ["x", "mean_keepdim_count", "mean"]
-    pending = [None] * RES_SLOTS
     fold = None
-    tot = res
     fold_note = None
     if world > 1 and args.collective == "fold":
         fold, fold_note = _peer_fold(rank, world)
-        if fold is not None:
-            tot = torch.zeros(RES_SLOTS, 2, device=dev, dtype=torch.float32)
+    # result slots: step i writes slot i % slots, so the exchange of step i overlaps the
+    # kernels of the next steps; before a slot is written again the exchange that read it
+    # has completed (an all-reduce is waited for on the stream; a fold's completion event is
+    # waited for unless it has already fired), and all are settled before the stop event
+    slots = FOLD_SLOTS if fold is not None else RES_SLOTS
+    res = torch.zeros(slots, 2, device=dev, dtype=torch.float32)
+    tot = torch.zeros(slots, 2, device=dev, dtype=torch.float32) if fold is not None else res
+    stream = torch.cuda.current_stream(dev)
+    sh = stream.cuda_stream
+    # the fold runs on a stream of its own, after an event behind each step's mean: in the
+    # stream of overlapped reductions it would sit between the mean and the next sum, whose
+    # writes would then wait for the slowest rank's flag (measured on 4 GPUs, us per step,
+    # two boxes: no exchange 72.0 / 72.0, fold in the stream 76.0 / 73.6, fold on its own
+    # stream 72.5 / 72.5; an event wait between two overlapped launches cost nothing, 72.0)
+    side = torch.cuda.Stream(device=dev) if fold is not None else None
+    mean_done = [torch.cuda.Event() for _ in range(slots)] if fold is not None else None
+    fold_ev = [torch.cuda.Event() for _ in range(slots)] if fold is not None else None
+    fold_done = [None] * slots
+    grid3, block3 = k_s["grid"], k_s["block"]
+    p_sum = [[x.data_ptr(), res[i].data_ptr()] for i in range(slots)]
+    p_mean = [[x.data_ptr(), count.data_ptr(), res[i].data_ptr() + 4] for i in range(slots)]
+    assert [a["name"] for a in k_m["args"]] == ["x", "mean_keepdim_count", "mean"]
+    pending = [None] * slots
+    last_fold = [None]
+    align = torch.zeros(2, device=dev, dtype=torch.float32)    # the untimed aligning exchange
     overlap_ok = world == 1 or fold is not None
 
     def drain():
+        """Every exchange issued so far completes before what is enqueued next on the stream."""
         for i, h in enumerate(pending):
             if h is not None:
                 h.wait()
                 pending[i] = None
+        if last_fold[0] is not None:
+            stream.wait_event(last_fold[0])
+            last_fold[0] = None
 
-    def step(i, ev=None, collective=True):
+    def step(i, ev=None, collective=True, lead=False):
         """One step: sum and mean kernels, then (N > 1) the sum of the two scalars over ranks.
         Untimed heat-up and tail steps, whose count follows the wall clock and so differs
         between ranks, skip it: every rank issues the same collectives in the same order.
@@ -295,20 +310,26 @@ def run_ours(args, rank, world, local_rank):
         first without sharing any line with its predecessor: x is read from HBM by each
         kernel (268 MB, twice L2).
         With N > 1 the fold kernel (emmy_rt_fold_f32, one warp) sums the scalars over ranks
-        through peer stores into every rank's mailbox; it is launched overlapped too, lets the
-        next step's sum start at once and takes no SM room the reductions need. The NCCL
+        through peer stores into every rank's mailbox, on its own stream once the step's mean
+        has completed; it takes no SM room the reductions need. The NCCL
         alternative (--collective nccl) runs with plain launches and an async all-reduce:
         measured at N = 2 (us per step), plain launches with it 85.5, overlapped launches with
         it 102.6 (its kernel competes for SMs with the overlapped reductions).
-        With ``ev`` (the per-kernel timing pass) they are plain launches between events."""
-        slot = i % RES_SLOTS
+        With ``ev`` (the per-kernel timing pass) they are plain launches between events.
+        ``lead``: the first step after the start event, whose sum starts only once everything
+        before the event has completed."""
+        slot = i % slots
         if pending[slot] is not None:
             pending[slot].wait()
             pending[slot] = None
+        if fold_done[slot] is not None:
+            if not fold_done[slot].query():          # the fold that read this slot
+                stream.wait_event(fold_done[slot])
+            fold_done[slot] = None
         if ev:
             ev[0].record(stream)
         overlap = not ev and overlap_ok
-        mod_s.launch(grid3, block3, 0, p_sum[slot], sh, overlap=overlap)
+        mod_s.launch(grid3, block3, 0, p_sum[slot], sh, overlap=overlap and not lead)
         if ev:
             ev[1].record(stream)
         mod_m.launch(grid3, block3, 0, p_mean[slot], sh, overlap=overlap)
@@ -316,7 +337,12 @@ def run_ours(args, rank, world, local_rank):
             ev[2].record(stream)
         if world > 1 and collective:
             if fold is not None:
-                fold.launch(res[slot].data_ptr(), 2, tot[slot].data_ptr(), sh, overlap=not ev)
+                mean_done[slot].record(stream)
+                side.wait_event(mean_done[slot])
+                fold.launch(res[slot].data_ptr(), 2, tot[slot].data_ptr(), side.cuda_stream,
+                            overlap=False)
+                fold_done[slot] = last_fold[0] = fold_ev[slot]
+                fold_done[slot].record(side)
             else:
                 pending[slot] = dist.all_reduce(res[slot], async_op=True)
 
@@ -358,10 +384,19 @@ def run_ours(args, rank, world, local_rank):
         start = torch.cuda.Event(enable_timing=True)
         stop = torch.cuda.Event(enable_timing=True)
         t0 = clocks.mark()
+        if world > 1:
+            # ranks leave the host barrier tens of microseconds apart, and the first timed
+            # exchange would charge that skew to the ranks that started early: one untimed
+            # exchange on the stream lines the ranks up on the device (every rank leaves it
+            # within one NVLink flag round trip) and the start event follows it
+            if fold is not None:
+                fold.launch(res[0].data_ptr(), 2, align.data_ptr(), sh, overlap=False)
+            else:
+                dist.all_reduce(align)
         start.record(stream)
         h0 = time.perf_counter()
         for i in range(args.steps):
-            step(i)
+            step(i, lead=i == 0)
         host_us_step = (time.perf_counter() - h0) / args.steps * 1e6   # enqueue time only
         drain()
         stop.record(stream)
@@ -379,10 +414,13 @@ def run_ours(args, rank, world, local_rank):
     ms = ms_local = start.elapsed_time(stop)
     sum_us = [e[0].elapsed_time(e[1]) * 1e3 for e in evs]
     mean_us = [e[1].elapsed_time(e[2]) * 1e3 for e in evs]
+    rank_ms = [ms]
     if world > 1:
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        t = torch.zeros(world, device=dev, dtype=torch.float64)
+        t[rank] = ms
+        dist.all_reduce(t)                  # every rank's timed region, max taken below
+        rank_ms = [round(float(v), 5) for v in t.tolist()]
+        ms = max(rank_ms)
     ms_step = ms / args.steps
 
     bytes_sum = 4 * N_REDUCE + 4
@@ -442,6 +480,7 @@ def run_ours(args, rank, world, local_rank):
                   **({"fold_error_word": fold_err} if fold is not None else {}),
                   **({"fold_unavailable": fold_note} if fold_note else {})},
         "host_enqueue_us_per_step": round(host_us_step, 2),
+        "rank_ms": rank_ms,          # each rank's timed region (device events); value uses the max
         "gpu_launches": (3 if fold is not None else 2) * args.steps,
         "e2e": e2e,
         "clocks": clocks.summary(t0, t1),

@@ -18,6 +18,12 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a B200 (runs the emitted PTX through libemmyrt)")
 
 
+def pytest_addoption(parser):
+    parser.addoption("--synth-seeds", type=int, default=None,
+                     help="seeds per family for the synthesized-IR GPU checks "
+                          "(tests/test_gpu_synth.py; default 24-40 per family)")
+
+
 def problem_dirs():
     return sorted(p for p in PROBLEMS.iterdir() if (p / "meta.json").is_file())
 

@@ -16,7 +16,16 @@ from test_synth import _fp64
 
 pytestmark = pytest.mark.gpu
 
-SEEDS = range(40)
+# seeds per test by default; ``pytest --synth-seeds N`` runs N seeds of every family
+DEFAULT_SEEDS = {"test_pointwise": 40, "test_rows_and_reductions": 40, "test_contraction": 40,
+                 "test_contraction_template": 32, "test_contraction_ragged_edges": 24,
+                 "test_attention": 24}
+
+
+def pytest_generate_tests(metafunc):
+    if "seed" in metafunc.fixturenames:
+        n = metafunc.config.getoption("synth_seeds") or DEFAULT_SEEDS[metafunc.function.__name__]
+        metafunc.parametrize("seed", range(n))
 
 
 def _close(got, ref, rel, label=None):
@@ -29,7 +38,6 @@ def _close_rows(info, got, ref):
     return tol.elementwise(got, ref, 1e-5, floor=floor, label=f"synth {kind}")[0]
 
 
-@pytest.mark.parametrize("seed", SEEDS)
 def test_pointwise(seed, gpu_runtime):
     from emmyptx import synth
     from emmyptx.emit import compile_payload
@@ -53,7 +61,6 @@ def test_pointwise(seed, gpu_runtime):
     assert np.all(np.abs(g - w) <= 1e-4 * np.abs(w) + 1e-5 * scale), info
 
 
-@pytest.mark.parametrize("seed", SEEDS)
 def test_rows_and_reductions(seed, gpu_runtime):
     from emmyptx import synth
     from emmyptx.emit import compile_payload
@@ -67,7 +74,6 @@ def test_rows_and_reductions(seed, gpu_runtime):
         assert _close_rows(info, got, _fp64(info, inputs)), (template, info)
 
 
-@pytest.mark.parametrize("seed", SEEDS)
 def test_contraction(seed, gpu_runtime):
     from emmyptx import synth
     from emmyptx.emit import compile_payload
@@ -81,7 +87,6 @@ def test_contraction(seed, gpu_runtime):
     assert _close(got, want, 1e-4, label=f"synth matmul {template}"), (template, info)
 
 
-@pytest.mark.parametrize("seed", range(32))
 def test_contraction_template(seed, gpu_runtime):
     """Random shapes inside the tcgen05 template's conditions with the template forced: CTA
     pairs, single CTAs, several tiles per CTA or cluster, half-width units; error word 0
@@ -98,7 +103,6 @@ def test_contraction_template(seed, gpu_runtime):
     assert _close(got, want, 1e-4, label="synth matmul tcgen05 forced"), info
 
 
-@pytest.mark.parametrize("seed", range(24))
 def test_contraction_ragged_edges(seed, gpu_runtime):
     """Shapes that are not multiples of the tcgen05 tile (M of 128, N of the tile width, K of
     32) on the template, with the edge tiles masked: zero-filled loads past the matrix, no
@@ -117,7 +121,6 @@ def test_contraction_ragged_edges(seed, gpu_runtime):
     assert _close(got, want, 1e-4, label="synth matmul ragged tcgen05"), info
 
 
-@pytest.mark.parametrize("seed", range(24))
 def test_attention(seed, gpu_runtime):
     from emmyptx import synth
     from emmyptx.emit import compile_payload
