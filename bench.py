@@ -744,12 +744,6 @@ def measure_config(name, args, peaks, l2, flush, *, device=0, compile_repeats=5,
                              "achieved": round(tfl, 2), "peak": round(ceil, 1),
                              "unit": "TFLOP/s", "frac": round(tfl / ceil, 4),
                              "peak_source": f"{peaks['source']} {TENSOR_DENOM}"}
-        if peaks.get("bf16_tflops_sustained"):
-            # the launches run back to back for a few hundred ms under the 1 kW power limit:
-            # the same ceiling from the GEMM rate held for seconds, for context
-            sus = peaks["bf16_tflops_sustained"] / 2.0 / 3.0
-            entry["roofline"]["peak_sustained"] = round(sus, 1)
-            entry["roofline"]["frac_of_sustained"] = round(tfl / sus, 4)
     if cpu:
         from oracle import cpu_baseline as cb
         entry["cpu_baseline"] = cb.workload_baseline(

@@ -165,6 +165,59 @@ def test_fold_overlapped_behind_emitted_sum(gpu_runtime):
     xb.free()
 
 
+def test_fold_on_its_own_stream_behind_the_reductions(gpu_runtime):
+    """The benchmark's exchange pattern: overlapped sum -> mean launches on one stream, each
+    step's fold on a second stream after an event recorded behind that step's mean, every step
+    writing its own result slot. Each folded pair equals the pair the kernels wrote (so no fold
+    read a slot before its mean completed), and the sum matches fp64."""
+    import torch
+    from emmyptx import workloads
+    from emmyptx.emit import compile_payload
+    rt = gpu_runtime
+    dev = torch.device("cuda", 0)
+    n = (1 << 22) + 3
+    g = torch.Generator(device=dev).manual_seed(3)
+    x = torch.empty(n, device=dev, dtype=torch.float32).uniform_(-1, 1, generator=g)
+    cnt = torch.tensor([float(n)], device=dev, dtype=torch.float32)
+    mods = []
+    for op in ("sum", "mean"):
+        payload, meta = workloads.full_reduce(n, op, grid=592)
+        ptx, _, _ = compile_payload(payload, meta)
+        k = meta["kernels"][0]
+        mods.append((rt.Module(ptx, k["entry"]), k))
+    (ms, ks), (mm, km) = mods
+    assert [a["name"] for a in km["args"]] == ["x", "mean_keepdim_count", "mean"]
+    f = _Fold(rt, 1)
+    L = rt.lib()
+    steps = 12
+    res = torch.zeros(steps, 2, device=dev, dtype=torch.float32)
+    tot = torch.full((steps, 2), float(SENTINEL), device=dev, dtype=torch.float32)
+    main, side = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    evs = [torch.cuda.Event() for _ in range(steps)]
+    torch.cuda.synchronize()
+    for i in range(steps):
+        ms.launch(ks["grid"], ks["block"], 0, [x.data_ptr(), res[i].data_ptr()],
+                  main.cuda_stream, overlap=i > 0)
+        mm.launch(km["grid"], km["block"], 0, [x.data_ptr(), cnt.data_ptr(), res[i].data_ptr() + 4],
+                  main.cuda_stream, overlap=True)
+        evs[i].record(main)
+        side.wait_event(evs[i])
+        rc = L.emmy_rt_fold_f32(res[i].data_ptr(), 2, f.ptrs.ptr, 0, 1, i + 1, tot[i].data_ptr(),
+                                f.err.ptr, side.cuda_stream, 0)
+        assert rc == 0, L.emmy_rt_last_error()
+    torch.cuda.synchronize()
+    got, wrote = tot.cpu().numpy(), res.cpu().numpy()
+    assert np.array_equal(got, wrote)
+    assert np.all(got == got[0])
+    want = float(x.double().sum())
+    assert abs(float(got[0, 0]) - want) <= 1e-5 * abs(want) + 1e-5 * n ** 0.5
+    assert abs(float(got[0, 1]) - want / n) <= 1e-5 * abs(want / n) + 1e-5 / n ** 0.5
+    assert ms.error_word() == 0 and mm.error_word() == 0 and f.error() == 0
+    ms.close()
+    mm.close()
+    f.free()
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
