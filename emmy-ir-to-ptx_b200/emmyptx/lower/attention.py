@@ -14,27 +14,29 @@ Warp roles (256 threads):
   ``tcgen05.st`` (the S product reads A from TMEM); per key block read S with
   ``tcgen05.ld``, run the online softmax in registers (base-2 exponentials,
   log2(e) folded into the scale, one FFMA + ``ex2`` per score), and write
-  P_hi / P_lo to shared memory (K-major SWIZZLE_128B). The output accumulator
+  P_hi / P_lo to tensor memory with ``tcgen05.st`` (D = 32, 64, 128), or to shared memory
+  in the K-major SWIZZLE_128B layout where tensor memory has no room for it
+  (D = 96). The output accumulator
   O stays in tensor memory; the running maximum is only raised when a row's
   block maximum exceeds it by more than 2^8 (then that warp rescales its O rows
   in TMEM), so most blocks need no correction at all. The next work item's Q
   rows are fetched during the last key block and stored as soon as the last S
   product has landed. Finally O / l is stored;
 * warp 4: one ``elect.sync`` lane issues S_j = Q K_j^T (A in TMEM, B in shared
-  memory) into one of two S buffers and O += P_j V_j (both operands in shared
-  memory); S runs one block ahead of P*V so the tensor core overlaps the
-  softmax;
+  memory) into one of two S buffers and O += P_j V_j (A = P in tensor or shared
+  memory, B in shared memory); S runs one block ahead of P*V so the tensor core
+  overlaps the softmax;
 * warps 5-7: fill the kt and v tiles of each key block, MN-major in
   SWIZZLE_128B_BASE32B (the TF32 MN-major layout). When the runtime has written
   tensor maps for the launch's kt and v pointers, warp 5 copies each raw tile
   with ``cp.async.bulk.tensor`` (the raw f32 words serve as the hi operand: the
   MMA reads their top 19 bits) and warps 6-7 write the lo tile from it; with one
-  buffer per tile (D = 128) the MMA warp issues the products that read only the
-  raw tile (hi x hi, lo x hi) as soon as the copy lands and the hi x lo products
-  once the lo tile is written. Otherwise all three warps load
-  the tiles with 16-byte loads (the next kt tile in flight while the v tile
-  waits for its buffer), split them and store hi and lo. Both paths give the same
-  bits.
+  buffer per tile (D = 96, or a launch whose shared memory holds only one) the
+  MMA warp issues the products that read only the raw tile (hi x hi, lo x hi) as
+  soon as the copy lands and the hi x lo products once the lo tile is written.
+  Otherwise all three warps load the tiles with 16-byte loads (the next kt tile in
+  flight while the v tile waits for its buffer), split them and store hi and lo.
+  Both paths give the same bits.
 
 Hand-offs use mbarriers (loads -> MMA, MMA commit -> softmax, softmax -> MMA);
 every wait is bounded and warp-uniform; on expiry it sets bit 3 of
@@ -75,8 +77,9 @@ def smem_bytes_needed(D, nbuf=1):
 
 
 def tile_buffers(D, smem):
-    """kt/v tile buffers: two at D = 32 and 64 when the launch's shared memory holds them (a
-    tile can then be stored while the tensor core still reads the other), else one."""
+    """kt/v tile buffers: two when the launch's shared memory holds them (a tile can then be
+    stored while the tensor core still reads the other), else one; always one at D = 96, whose
+    P takes shared memory too."""
     return 2 if D != 96 and smem >= smem_bytes_needed(D, 2) else 1
 
 
@@ -348,9 +351,10 @@ def lower_attention(gen, kernel, plan):
     # tensor memory columns: Q_hi, Q_lo, two S buffers, the O accumulator
     c.update(QHI=0, QLO=D, S0=2 * D, O=2 * D + 2 * BKV)
     TMEM_COLS = 512
-    # P in tensor memory when it fits (D = 64: Q 128 + S 128 + O 64 + P hi/lo 128 columns):
-    # the softmax writes it with tcgen05.st and P*V reads A from TMEM; otherwise (D = 128)
-    # P goes through shared memory in the K-major SWIZZLE_128B layout
+    # P in tensor memory when it fits (D = 64: Q 128 + S 128 + O 64 + P hi/lo 128 columns;
+    # D = 128 with 32-key blocks: 256 + 64 + 128 + 64): the softmax writes it with tcgen05.st
+    # and P*V reads A from TMEM; otherwise (D = 96) P goes through shared memory in the
+    # K-major SWIZZLE_128B layout
     c["P_TMEM"] = _p_in_tmem(D, BKV)
     c.update(PTHI=3 * D + 2 * BKV, PTLO=3 * D + 3 * BKV)
     # dynamic shared memory (1024-aligned): NBUF x (kt hi, kt lo), NBUF x (v hi, v lo), P hi/lo
@@ -385,7 +389,7 @@ def lower_attention(gen, kernel, plan):
     # On the TMA path the producer lane arrives for its warp once it has issued a tile's copy,
     # and KRAW[b] / VRAW[b] complete when the raw kt / v tile has landed (expect_tx); the
     # workers arrive on SGO / PVGO once the lo tile is written. With one buffer per tile
-    # (D = 128) the copies are on the critical path: the producer then arrives for all 96 on
+    # (D = 96) the copies are on the critical path: the producer then arrives for all 96 on
     # SGO / PVGO, the MMA warp issues the products that read only the raw tile (hi x hi,
     # lo x hi) after KRAW / VRAW and the hi x lo products after KLO[b] / VLO[b] (64 worker
     # arrivals once the lo tile is written).
@@ -1030,7 +1034,7 @@ def _load_tma(gen, plan, tid, base, B, wait, cta, ncta, c):
     hi buffer with ``cp.async.bulk.tensor`` (one box per 32-column strip, completing on the
     KRAW / VRAW barrier pair; no multicast, the maps cover this GPU's buffers only) and
     arrives for its warp on SGO / PVGO (for all 96 loader threads when the products are split
-    around the lo pass, D = 128). Warps 6-7 wait for the copy, write the lo tile and arrive on
+    around the lo pass: one buffer per tile, D = 96). Warps 6-7 wait for the copy, write the lo tile and arrive on
     SGO / PVGO (KLO / VLO when split). The tile order is the register path's: kt of block
     J + 1 before v of block J.
     On an expired wait the producer waits (bounded) for the copies it has in flight before it
