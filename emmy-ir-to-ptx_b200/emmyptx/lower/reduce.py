@@ -31,7 +31,9 @@ widened (exactly) and added in f64, a thread of the full reduction keeps one
 f64 accumulator per chunk in flight (short dependent chains), and the warp
 ladder, the cross-warp tree and the cross-CTA fold add in f64; the result is
 rounded to f32 once, before the IR's own scalar program (the mean's
-division) runs. An f32 accumulation of n terms is off by about
+division) runs. A full reduction whose launch gives each thread at most
+``F32_LANE_LIMIT`` elements first adds them in f32 into 16 lane registers per
+thread (at most 64 terms each) and widens those once (see ``_lower_full``). An f32 accumulation of n terms is off by about
 2^-24 * sum|x| (times a factor that grows with n) whatever its order, and so
 is Kahan's compensated loop (its bound is 2^-23 * sum|x|): both exceed
 1e-5 * |sum x| when the sum is small next to sum|x|. Measured on B200 for the
