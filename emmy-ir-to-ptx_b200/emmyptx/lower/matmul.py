@@ -4,7 +4,8 @@ The IR describes matmul as a per-thread FMA schedule over a ``cp.async``
 ring (reference ``problems/m01_matmul_512``, ``m02_matmul_rect``; lowered
 statement by statement by reference ``compile.py:4858-5579``). On B200 the
 template keeps only the contraction and computes it with
-``tcgen05.mma.cta_group::1.kind::tf32`` into a tensor-memory accumulator.
+``tcgen05.mma.kind::tf32`` (``cta_group::1``, or ``::2`` for CTA pairs) into a
+tensor-memory accumulator.
 
 f32 accuracy with TF32 inputs (3xTF32, Ootomo & Yokota 2022): each operand
 x is split into ``hi`` (x with its 13 low mantissa bits cleared, an integer
@@ -26,6 +27,15 @@ CTA tile 128 x BN (BN <= 256), K step 32 (one 128-byte swizzle atom of f32):
 * warps 0-3 drain the 128 x BN accumulator with ``tcgen05.ld.32x32b``
   (warp w owns TMEM lanes 32w..32w+31, one output row per thread) and store
   it (``red.global.add.f32`` when the IR's write is atomic).
+
+CTA pairs (even grid, M % 256 = 0, dynamic shared memory for two stages: the
+benchmark shapes): the PTX declares clusters of two CTAs, each loading 128 rows
+of A and half of the B tile's columns; the leader issues
+``tcgen05.mma.cta_group::2`` with M = 256, which reads both CTAs' shared memory
+and writes each CTA's rows into its own tensor memory, so each SM stages half of
+B. The first ``SM_COUNT / 2`` clusters walk 256 x BN tiles; the tiles of an
+incomplete last round run as half-width units. Ragged M, N and K (multiples of 4)
+are masked: chunks outside the matrix are zero-filled, stores stop at its edge.
 
 Stages ``S`` and ``BN`` are chosen from the shared memory the launch provides
 (``meta.json`` ``smem_bytes`` is dynamic shared memory; without it the stages
