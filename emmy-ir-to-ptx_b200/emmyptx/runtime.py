@@ -134,6 +134,26 @@ def init(device: int | None = None):
     if device not in _initialised:
         check(lib().emmy_rt_init(device))
         _initialised.add(device)
+        _note_sm_count(device)
+
+
+B200_SM_COUNT = 148
+
+
+def _note_sm_count(device: int):
+    """The emitted PTX sizes some work splits for B200's 148 SMs (the matmul's working CTA
+    pairs, the benchmark's default reduction grid of 4 CTAs per SM). Every kernel stays
+    correct on another SM count (all walk their work grid-stride), but the split is then not
+    the tuned one: say so once per device instead of silently running it."""
+    try:
+        sm = device_info(device)["sm_count"]
+    except RuntimeError:
+        return
+    if sm != B200_SM_COUNT:
+        import warnings
+        warnings.warn(f"device {device} has {sm} SMs; the emitted kernels' work splits are "
+                      f"sized for B200's {B200_SM_COUNT} (results stay correct, the split is "
+                      "not the tuned one)", RuntimeWarning, stacklevel=3)
 
 
 def device_info(device: int = 0) -> dict:

@@ -29,3 +29,26 @@ def test_abi_version_and_error_path():
         rc = L.emmy_rt_init(0)
         assert rc != 0
         assert L.emmy_rt_last_error()
+
+
+class _FakeLib:
+    def emmy_rt_init(self, device):
+        return 0
+
+
+def test_init_notes_a_device_that_is_not_a_b200(monkeypatch):
+    """Initialising a device whose SM count differs from B200's warns once (the emitted work
+    splits are sized for 148 SMs) and stays silent on a B200; no GPU needed (fake library)."""
+    import warnings
+
+    import pytest
+    monkeypatch.setattr(runtime, "lib", lambda: _FakeLib())
+    monkeypatch.setattr(runtime, "_initialised", set())
+    monkeypatch.setattr(runtime, "device_info", lambda d: {"sm_count": 132})
+    with pytest.warns(RuntimeWarning, match="132 SMs"):
+        runtime.init(3)
+    with warnings.catch_warnings():
+        warnings.simplefilter("error")
+        runtime.init(3)                                  # already initialised: no second note
+        monkeypatch.setattr(runtime, "device_info", lambda d: {"sm_count": 148})
+        runtime.init(4)
