@@ -25,17 +25,22 @@ def _ptxas(ptx, tmp_path):
 
 
 @pytest.mark.parametrize("family", ["pointwise", "rows", "reduction", "contraction",
-                                    "attention"])
+                                    "contraction_tc", "contraction_ragged", "attention"])
 def test_synthesized_kernels_lower_and_assemble(family, tmp_path):
     templates = set()
+    # the forced-template families (pairs, half-width units, split-K, masked edges) are
+    # compiled as their GPU tests compile them
+    force = "contraction" if family in ("contraction_tc", "contraction_ragged") else None
     for seed in SEEDS:
         payload, meta, info = getattr(synth, family)(seed)
-        ptx, template, _ = compile_payload(payload, meta)
+        ptx, template, _ = compile_payload(payload, meta, template=force)
         assert ".target sm_100a" in ptx
         _ptxas(ptx, tmp_path)
         templates.add(template)
     if family == "contraction":           # both the tcgen05 template and the walker occur
         assert templates == {"contraction", "walker"}
+    if force:
+        assert templates == {"contraction"}
     if family == "attention":             # tcgen05, the warp-per-row template and the walker
         assert templates == {"attention", "attention_warp", "walker"}
 
