@@ -25,7 +25,7 @@ Under a plain launch both instructions do nothing.
 
 from __future__ import annotations
 
-from ..analysis import ElemLoad, ElemWrite
+from ..analysis import ElemLoad
 from ..codegen import run_program
 from .common import addr, aligned_predicate, load_pointers
 

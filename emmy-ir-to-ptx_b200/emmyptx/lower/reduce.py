@@ -48,7 +48,7 @@ spinning forever.
 
 from __future__ import annotations
 
-from ..analysis import ElemAccum, ElemLoad, ElemOp, ElemWrite, IDENTITY
+from ..analysis import ElemAccum, ElemLoad, ElemWrite
 from ..codegen import emit_op, identity_literal, run_program
 from .common import WAIT_LIMIT, aligned_predicate, load_pointers
 
