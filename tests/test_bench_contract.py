@@ -30,3 +30,19 @@ def test_reference_arm_prints_one_contract_line():
 def test_bench_rejects_fewer_than_three_warmup_steps_by_raising_them():
     src = (ROOT / "bench.py").read_text()
     assert "args.warmup = max(args.warmup, 3)" in src
+
+
+def test_clock_summary_reads_the_sampled_fields():
+    """The clock sampler's summary (no GPU: lines as nvidia-smi prints them with nounits)."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("bench_mod", ROOT / "bench.py")
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    s = bench.ClockSampler(0)
+    s.lines = [(10.0, "0, 1680, 1965, 702.5, 0x4, Not Active, Not Active, Not Active, Active"),
+               (10.2, "0, 1700, 1965, 710.1, 0x4, Not Active, Not Active, Not Active, Active"),
+               (10.4, "0, 1690, 1965, 706.0, 0x4, Not Active, Not Active, Not Active, Active"),
+               (99.0, "0, 120, 1965, 199.0, 0x1, Not Active, Not Active, Not Active, Not Active")]
+    out = s.summary(10.1, 10.3)
+    assert out["samples"] == 3 and out["sm_mhz"] == 1690.0 and out["sm_max_mhz"] == 1965.0
+    assert out["reasons"] == ["sw_power_cap"] and out["power_w"] == 706.0
