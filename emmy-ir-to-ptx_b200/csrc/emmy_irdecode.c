@@ -18,12 +18,18 @@
  * _irdecode.Fallback, and a grammar error inside it raises the IRDecodeError
  * given to setup(); ir.py then decodes the statement with its Python decoders,
  * which are the reference for the result and for the error messages.
+ *
+ * Values nest at most MAX_DEPTH levels (real bodies nest a few tens): the parser
+ * recurses once per level, and a deeper text raises Fallback before the C stack
+ * could overflow, so a malformed IR file ends in a decode error, not a crash.
  */
 #define PY_SSIZE_T_CLEAN
 #include <Python.h>
 
 #include <stdlib.h>
 #include <string.h>
+
+#define MAX_DEPTH 1000
 
 static PyObject *g_classes;   /* name -> class */
 static PyObject *g_fields;    /* name -> tuple of field names */
@@ -35,6 +41,7 @@ static PyObject *g_empty;     /* () */
 typedef struct {
   const char *s;
   Py_ssize_t n, i;
+  int depth;      /* values being parsed around the current position */
   PyObject *memo; /* call text -> node */
 } P;
 
@@ -80,6 +87,7 @@ static PyObject *parse_seq(P *p, char close) {
   p->i++; /* opening bracket */
   PyObject *list = PyList_New(0);
   if (!list) return NULL;
+  int trailing_comma = 0;
   for (;;) {
     skip_ws(p);
     if (p->i >= p->n) {
@@ -90,6 +98,7 @@ static PyObject *parse_seq(P *p, char close) {
       p->i++;
       break;
     }
+    trailing_comma = 0;
     PyObject *v = parse_value(p);
     if (!v) {
       Py_DECREF(list);
@@ -104,10 +113,17 @@ static PyObject *parse_seq(P *p, char close) {
     skip_ws(p);
     if (p->i < p->n && p->s[p->i] == ',') {
       p->i++;
+      trailing_comma = 1;
     } else if (p->i >= p->n || p->s[p->i] != close) {
       Py_DECREF(list);
       return fallback("malformed sequence");
     }
+  }
+  /* '(v)' is v itself in Python but a one-element list on the JSON path: a repr never
+     writes it, so the Python decoders decide */
+  if (close == ')' && PyList_GET_SIZE(list) == 1 && !trailing_comma) {
+    Py_DECREF(list);
+    return fallback("parenthesized value");
   }
   PyObject *t = PyList_AsTuple(list);
   Py_DECREF(list);
@@ -129,14 +145,20 @@ static PyObject *parse_string(P *p) {
 static PyObject *parse_number(P *p) {
   Py_ssize_t a = p->i;
   int is_float = 0;
-  if (p->s[p->i] == '-' || p->s[p->i] == '+') p->i++;
-  if (p->i < p->n && is_ident_start(p->s[p->i])) { /* -inf, -nan */
+  /* the grammar a repr writes: digits, '-' digits, -inf, -nan; a '+' sign, a lone '-' and
+     leading zeros (which Python refuses in integers) are left to the Python decoders */
+  if (p->s[p->i] == '+') return fallback("plus sign");
+  if (p->s[p->i] == '-') p->i++;
+  if (p->i >= p->n || !(is_ident_start(p->s[p->i]) || (p->s[p->i] >= '0' && p->s[p->i] <= '9')))
+    return fallback("sign without a number");
+  if (p->s[p->i] == '0' && p->i + 1 < p->n && p->s[p->i + 1] >= '0' && p->s[p->i + 1] <= '9')
+    return fallback("leading zero");
+  if (is_ident_start(p->s[p->i])) { /* -inf, -nan */
     Py_ssize_t b = p->i;
     while (p->i < p->n && is_ident(p->s[p->i])) p->i++;
     Py_ssize_t len = p->i - b;
-    double sign = p->s[a] == '-' ? -1.0 : 1.0;
-    if (len == 3 && !memcmp(p->s + b, "inf", 3)) return PyFloat_FromDouble(sign * Py_HUGE_VAL);
-    if (len == 3 && !memcmp(p->s + b, "nan", 3)) return PyFloat_FromDouble(Py_NAN);
+    if (len == 3 && !memcmp(p->s + b, "inf", 3)) return PyFloat_FromDouble(-Py_HUGE_VAL);
+    if (len == 3 && !memcmp(p->s + b, "nan", 3)) return PyFloat_FromDouble(-Py_NAN);
     return fallback("signed name");
   }
   while (p->i < p->n) {
@@ -310,7 +332,7 @@ done:
   return result;
 }
 
-static PyObject *parse_value(P *p) {
+static PyObject *parse_value_at(P *p) {
   skip_ws(p);
   if (p->i >= p->n) return fallback("unexpected end");
   char c = p->s[p->i];
@@ -335,6 +357,14 @@ static PyObject *parse_value(P *p) {
   return fallback("unexpected character");
 }
 
+static PyObject *parse_value(P *p) {
+  if (p->depth >= MAX_DEPTH) return fallback("nesting too deep");
+  p->depth++;
+  PyObject *v = parse_value_at(p);
+  p->depth--;
+  return v;
+}
+
 static PyObject *py_setup(PyObject *self, PyObject *args) {
   PyObject *classes, *fields, *defaults, *err;
   if (!PyArg_ParseTuple(args, "O!O!O!O", &PyDict_Type, &classes, &PyDict_Type, &fields,
@@ -354,6 +384,7 @@ static PyObject *py_decode(PyObject *self, PyObject *arg) {
   p.s = (const char *)PyUnicode_1BYTE_DATA(arg);
   p.n = PyUnicode_GET_LENGTH(arg);
   p.i = 0;
+  p.depth = 0;
   p.memo = PyDict_New();
   if (!p.memo) return NULL;
   PyObject *v = parse_value(&p);

@@ -201,8 +201,12 @@ def _convert(node):
         return tuple(_convert(e) for e in node.elts)
     if isinstance(node, ast.UnaryOp) and isinstance(node.op, ast.USub) \
             and isinstance(node.operand, ast.Constant) \
-            and isinstance(node.operand.value, (int, float)):
+            and isinstance(node.operand.value, (int, float)) \
+            and not isinstance(node.operand.value, bool):
         return -node.operand.value
+    if isinstance(node, ast.UnaryOp) and isinstance(node.op, ast.USub) \
+            and isinstance(node.operand, ast.Name) and node.operand.id in ("inf", "nan"):
+        return -float(node.operand.id)        # repr(float("-inf")) is "-inf"
     if isinstance(node, ast.Name) and node.id in ("inf", "nan"):
         return float(node.id)
     raise IRDecodeError(f"unsupported syntax in IR body: {ast.dump(node)[:80]}")
@@ -328,6 +332,13 @@ def decode_statement(text: str):
             value = None
         if isinstance(value, Node) and type(value).__name__ in STATEMENT_KINDS:
             return value
+    try:
+        return _decode_python(text)
+    except RecursionError:
+        raise IRDecodeError("KernelOp body nests too deeply") from None
+
+
+def _decode_python(text: str):
     fast = _fast_json(text)
     if fast is not None:
         try:
