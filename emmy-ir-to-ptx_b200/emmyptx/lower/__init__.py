@@ -73,6 +73,29 @@ class EmmyIRLowering:
         self.gen = PTXKernelGenerator(kernel)
         self.force = template
         self.template = None
+        self.values: dict = {}      # IR value name -> register, for :meth:`_assign`
+
+    def _assign(self, stmt) -> str:
+        """Lower one ``Assign`` statement on its own into :attr:`gen`, the way the
+        reference's op-table tests drive it (reference ``compile.py:2462-2594``): the
+        operands are registers already named in :attr:`values`, the result register is
+        stored under ``stmt.name`` and returned. An unknown operation raises
+        ``NotImplementedError`` ("Unsupported unary/binary elementwise operation")."""
+        from ..codegen import emit_op
+        from ..ir import dtype_name, op_name
+        op = stmt.op if isinstance(stmt.op, str) else getattr(stmt.op, "name", None)
+        if not isinstance(op, str):
+            op = op_name(stmt.op)
+        dt = getattr(stmt, "dtype", None)
+        dt = getattr(dt, "name", None) if dt is not None and not isinstance(dt, str) else dt
+        if dt not in (None, "f32"):
+            raise NotImplementedError(f"Unsupported elementwise dtype {dtype_name(dt)}")
+        try:
+            args = [self.values[a] for a in stmt.args]
+        except KeyError as exc:
+            raise ValueError(f"undefined elementwise input {exc.args[0]!r}") from None
+        self.values[stmt.name] = emit_op(self.gen, op, args)
+        return self.values[stmt.name]
 
     def _candidates(self):
         """(name, lift, emitter module) in dispatch order; a template module is imported

@@ -527,7 +527,8 @@ def _fold(op, a, b):
 def lower_general(gen, kernel):
     body = kernel.body
     if len(body) != 1 or type(body[0]).__name__ != "Tile":
-        raise NotImplementedError("kernel body must be a single Tile")
+        kinds = ", ".join(type(s).__name__ for s in body) or "nothing"
+        raise NotImplementedError(f"kernel body must be a single Tile, got {kinds}")
     tile = body[0]
     if getattr(tile, "aux_threads", 0):
         raise NotImplementedError("Auxiliary threads are not supported")

@@ -11,14 +11,17 @@ reference ``compile.py:1769-1994``) with the same error behaviour: exactly one
 from __future__ import annotations
 
 import json
+from dataclasses import dataclass
 from pathlib import Path
-from typing import Mapping, NamedTuple
+from typing import Mapping
 
 from .ir import IRDecodeError, graph_from_dict
 
 
-class EmmyKernelIR(NamedTuple):
-    """Validated kernel view (fields as reference ``compile.py:1770-1780``)."""
+@dataclass(frozen=True)
+class EmmyKernelIR:
+    """Validated kernel view: a frozen dataclass with the fields of reference
+    ``compile.py:1769-1780``, so ``dataclasses.replace`` derives a variant as it does there."""
 
     name: str
     body: tuple

@@ -15,14 +15,28 @@ Not restated, by design:
 * the register *declaration* lines (``.reg .u32 %r0;`` per register, reference
   ``tests/test_ptx_kernel_generator.py:80-106``): registers are declared in ranges
   (``.reg .b32 %r<2>;``), one line per register class. The register *names* the reference
-  expects are kept and checked below.
+  expects are kept and checked below;
+* the lowering tests' checks of the reference templates' own instruction text (reference
+  ``tests/test_emmy_ir_lowering.py``, ``test_emmy_reduction_lowering.py``,
+  ``test_emmy_rmsnorm_ptx.py``, ``test_emmy_softmax_lowering.py``,
+  ``test_emmy_l2norm_lowering.py``): counts of scalar ``ld.global.f32`` (these templates
+  load 16-byte vectors), ``add.f32`` (every add carries ``.rn``), ``max.f32``/``min.f32``
+  (``max.NaN``/``min.NaN``, which propagate NaN as numpy and PyTorch do), the reference's
+  label, shared-array and register names, its barrier and shuffle counts, and
+  ``.version 8.0`` (sm_100a needs a later PTX ISA). What those tests check about behaviour
+  (entry and parameters, one ``ret``, a cooperative reduction with warp shuffles and CTA
+  barriers, the op table's instruction per operation, fail-closed errors) is restated
+  below.
 """
 
 import json
 
 import pytest
 
-from compile import EmmyIRParser, EmmyKernelIR, PTXKernelGenerator
+from types import SimpleNamespace
+
+from compile import EmmyIRLowering, EmmyIRParser, EmmyKernelIR, PTXKernelGenerator
+from conftest import PROBLEMS
 
 _F32 = "DataType(name='f32', np=dtype('float32'), nbytes=4)"
 _BODY = ("Tile(axes=(Axis(name='a0', extent=Dim(4), window=None),), body=(Load(names=('v',), "
@@ -237,3 +251,87 @@ def test_args_must_match_arg_order(kernel):
     kernel.metadata["selected_kernel"]["args"] = [{"name": "x", "dtype": "f32", "shape": [1024]}]
     with pytest.raises(ValueError, match="do not match"):
         PTXKernelGenerator(kernel)
+
+
+# ---------------------------------------------------------------------------
+# EmmyIRLowering (reference tests/test_emmy_ir_lowering.py and the row-operation lowering
+# tests): the behaviour they check, on the reference's own fixtures
+# ---------------------------------------------------------------------------
+
+def _fixture(problem, entry):
+    return EmmyIRParser(PROBLEMS / problem / f"{entry}.ir.json", require_meta=True).parse()
+
+
+@pytest.fixture
+def pointwise():
+    return _fixture("p00_scalar_add", "k_add_pointwise")
+
+
+def test_pointwise_kernel_view(pointwise):
+    assert pointwise.name == "k_add_pointwise"
+    assert pointwise.arg_order == ("x0", "x1", "add")
+
+
+def test_pointwise_entry_parameters_and_single_ret(pointwise):
+    ptx = EmmyIRLowering(pointwise).lower()
+    assert ".visible .entry k_add_pointwise(" in ptx
+    for arg in ("x0", "x1", "add"):
+        assert f".param .u64 param_{arg}" in ptx
+        assert f"[param_{arg}]" in ptx
+    assert "ld.param.u64" in ptx
+    assert ptx.count("ret;") == 1
+    assert ptx.rstrip().endswith("}")
+
+
+@pytest.mark.parametrize("problem,entry", [("r01_array_sum", "k_sum_1_reduce"),
+                                           ("r03_mean", None),
+                                           ("f01_rmsnorm", None), ("f02_row_softmax", None),
+                                           ("f03_l2norm", None)])
+def test_cooperative_reductions_lower(problem, entry):
+    """Every reduction and row-normalisation fixture lowers to a kernel that reduces across
+    the CTA: warp shuffles and CTA barriers."""
+    if entry is None:
+        entry = next((PROBLEMS / problem).glob("*.ir.json")).name[:-len(".ir.json")]
+    kernel = _fixture(problem, entry)
+    ptx = EmmyIRLowering(kernel).lower()
+    assert f".visible .entry {kernel.name}(" in ptx
+    assert "shfl.sync.bfly.b32" in ptx
+    assert "bar.sync 0;" in ptx
+
+
+def test_unknown_statement_fails_naming_it(pointwise):
+    import dataclasses
+
+    class WarpMagic:
+        pass
+
+    broken = dataclasses.replace(pointwise, body=(WarpMagic(),))
+    with pytest.raises(NotImplementedError, match="WarpMagic"):
+        EmmyIRLowering(broken).lower()
+
+
+def _assign(lowering, op, args):
+    for a in args:
+        lowering.values[a] = lowering.gen.register(".f32")
+    stmt = SimpleNamespace(name="result", op=SimpleNamespace(name=op), args=args,
+                           dtype=SimpleNamespace(name="f32"))
+    lowering._assign(stmt)
+    assert "result" in lowering.values
+    return lowering.gen.render_entry()
+
+
+@pytest.mark.parametrize("op,args,instruction", [
+    ("negative", ("a",), "neg.f32"), ("absolute", ("a",), "abs.f32"),
+    ("identity", ("a",), "mov.f32"), ("sqrt", ("a",), "sqrt.rn.f32"),
+    ("rsqrt", ("a",), "rsqrt.approx.f32"), ("divide", ("a", "b"), "div.rn.f32"),
+    ("reciprocal", ("a",), "rcp.rn.f32"), ("exp", ("a",), "ex2.approx.f32"),
+    ("relu", ("a",), "max.NaN.f32"), ("maximum", ("a", "b"), "max.NaN.f32"),
+    ("minimum", ("a", "b"), "min.NaN.f32"), ("add", ("a", "b"), "add.rn.f32"),
+])
+def test_op_table_instruction(pointwise, op, args, instruction):
+    assert instruction in _assign(EmmyIRLowering(pointwise), op, args)
+
+
+def test_unknown_unary_operation_fails(pointwise):
+    with pytest.raises(NotImplementedError, match="Unsupported unary"):
+        _assign(EmmyIRLowering(pointwise), "unsupported_op", ("a",))
