@@ -544,6 +544,11 @@ def lower_general(gen, kernel):
                                             "CpAsyncCopy") for x in walk(tile.body))
     if cooperative and cells % B:
         raise NotImplementedError("cooperative Tile whose cells do not fill whole CTAs")
+    # the shuffles name all 32 lanes: a CTA that ends in a partial warp would have them wait
+    # on lanes that do not exist
+    if B % 32 and any(type(x).__name__ == "WarpShuffle" for x in walk(tile.body)):
+        raise NotImplementedError(f"WarpShuffle needs whole warps; the launch has {B} threads "
+                                  "per CTA")
 
     w = _Walker(gen, kernel)
     w.ptrs = load_pointers(gen, list(kernel.arg_order))

@@ -51,6 +51,23 @@ def test_unsupported_statement_fails_closed(tmp_path):
     assert "frobnicate" in r.stderr
 
 
+def test_warp_shuffle_with_a_partial_warp_fails_closed():
+    """r01's sum rescheduled for 48 threads per CTA (cells fill the CTA, but its second warp
+    has 16 lanes): the walker refuses it rather than emit a full-warp shuffle."""
+    from emmyptx.emit import compile_payload
+    pdir = PROBLEMS / "r01_array_sum"
+    payload = json.loads((pdir / "k_sum_1_reduce.ir.json").read_text())
+    node = payload["nodes"]["sum_1"]["op_fields"]
+    node["body"] = [b.replace("Dim(128)", "Dim(48)").replace("value=128", "value=48")
+                    for b in node["body"]]
+    meta = json.loads((pdir / "meta.json").read_text())
+    meta["kernels"][0]["block"] = [48, 1, 1]
+    with pytest.raises(NotImplementedError, match="WarpShuffle needs whole warps"):
+        compile_payload(payload, meta, template="walker")
+    with pytest.raises(NotImplementedError, match="whole"):
+        compile_payload(payload, meta)
+
+
 LOWERED = problem_dirs()
 
 
