@@ -524,6 +524,30 @@ def _fold(op, a, b):
     raise NotImplementedError(f"Index operator: {op}")
 
 
+def _check_convergence(stmts, under=None):
+    """Every thread of a CTA must reach each ``Sync`` (a CTA barrier) and every lane of a warp
+    each ``WarpShuffle`` (its mask names all 32 lanes). A barrier or shuffle inside a ``Cond``,
+    or inside a ``StridedLoop`` whose start, step or end names a variable (a trip count that
+    can differ between threads), could leave the threads that skip it waiting forever, so such
+    a body is refused rather than lowered. The IR forms seen so far keep them at the Tile's
+    top level or in loops with constant bounds."""
+    from ..analysis import _vars_in
+    for s in stmts:
+        kind = type(s).__name__
+        if kind in ("Sync", "WarpShuffle") and under:
+            raise NotImplementedError(f"{kind} inside {under}: not every thread is sure to "
+                                      "reach it")
+        if kind == "Cond":
+            _check_convergence(s.body, "a Cond")
+            _check_convergence(s.else_body, "a Cond")
+        elif kind == "StridedLoop":
+            varying = any(_vars_in(e) for e in (s.start, s.step, s.end) if e is not None)
+            _check_convergence(s.body, under or ("a StridedLoop with variable bounds"
+                                                 if varying else None))
+        elif kind in ("Loop", "Tile"):
+            _check_convergence(s.body, under)
+
+
 def lower_general(gen, kernel):
     body = kernel.body
     if len(body) != 1 or type(body[0]).__name__ != "Tile":
@@ -546,9 +570,20 @@ def lower_general(gen, kernel):
         raise NotImplementedError("cooperative Tile whose cells do not fill whole CTAs")
     # the shuffles name all 32 lanes: a CTA that ends in a partial warp would have them wait
     # on lanes that do not exist
-    if B % 32 and any(type(x).__name__ == "WarpShuffle" for x in walk(tile.body)):
+    if B % 32 and any(type(x).__name__ == "WarpShuffle" or (type(x).__name__ == "Sync"
+                                                          and x.warp)
+                      for x in walk(tile.body)):
         raise NotImplementedError(f"WarpShuffle needs whole warps; the launch has {B} threads "
                                   "per CTA")
+    for x in walk(tile.body):           # a barrier waits for its count of threads
+        if type(x).__name__ == "Sync" and not x.warp:
+            bid, count = int(x.barrier_id or 0), x.count
+            if not 0 <= bid <= 15:
+                raise NotImplementedError(f"barrier id {bid} outside the 16 CTA barriers")
+            if count and (int(count) % 32 or not 0 < int(count) <= B):
+                raise NotImplementedError(f"barrier count {count} is not a whole number of "
+                                          f"warps within the {B}-thread CTA")
+    _check_convergence(tile.body)
 
     w = _Walker(gen, kernel)
     w.ptrs = load_pointers(gen, list(kernel.arg_order))

@@ -68,6 +68,55 @@ def test_warp_shuffle_with_a_partial_warp_fails_closed():
         compile_payload(payload, meta)
 
 
+_SYNC = "Sync(barrier_id=0, count=None, warp=False)"
+_ACCUM = ("Accum(name='acc0', value='in0', op=ElementwiseImpl('add'), dtype=DataType(name='f32', "
+          "np=dtype('float32'), nbytes=4), axes=('a0',), base=None)")
+
+
+@pytest.mark.parametrize("old,new,where", [
+    (_SYNC, "Cond(cond=BinaryExpr(op='==', left=Var(name='lane'), right=Literal(value=0, "
+            f"dtype='int')), body=({_SYNC},), else_body=())", "a Cond"),
+    (_ACCUM, f"{_ACCUM}, {_SYNC}", "a StridedLoop with variable bounds"),
+])
+def test_barrier_off_the_convergent_path_fails_closed(old, new, where):
+    """r01's sum with its CTA barrier moved under a lane test, or into the strided loop whose
+    start is the thread's own index (trip counts differ between threads): refused, since a
+    thread that never reaches the barrier would leave the others waiting."""
+    from emmyptx.emit import compile_payload
+    pdir = PROBLEMS / "r01_array_sum"
+    payload = json.loads((pdir / "k_sum_1_reduce.ir.json").read_text())
+    node = payload["nodes"]["sum_1"]["op_fields"]
+    assert all(old in b for b in node["body"])
+    node["body"] = [b.replace(old, new) for b in node["body"]]
+    meta = json.loads((pdir / "meta.json").read_text())
+    for template in ("walker", None):
+        with pytest.raises(NotImplementedError, match=f"Sync inside {where}"):
+            compile_payload(payload, meta, template=template)
+
+
+@pytest.mark.parametrize("sync,refused", [
+    ("Sync(barrier_id=1, count=128, warp=False)", None),
+    ("Sync(barrier_id=16, count=None, warp=False)", "barrier id 16"),
+    ("Sync(barrier_id=1, count=256, warp=False)", "barrier count 256"),
+    ("Sync(barrier_id=1, count=48, warp=False)", "barrier count 48"),
+])
+def test_barrier_ids_and_counts(sync, refused):
+    """A CTA has 16 barriers, and a counted barrier waits for that many threads, in whole
+    warps: a count above the CTA's 128 threads would never be met."""
+    from emmyptx.emit import compile_payload
+    pdir = PROBLEMS / "r01_array_sum"
+    payload = json.loads((pdir / "k_sum_1_reduce.ir.json").read_text())
+    node = payload["nodes"]["sum_1"]["op_fields"]
+    node["body"] = [b.replace(_SYNC, sync) for b in node["body"]]
+    meta = json.loads((pdir / "meta.json").read_text())
+    if refused is None:
+        ptx, template, _ = compile_payload(payload, meta, template="walker")
+        assert "bar.sync 1, 128;" in ptx
+    else:
+        with pytest.raises(NotImplementedError, match=refused):
+            compile_payload(payload, meta, template="walker")
+
+
 LOWERED = problem_dirs()
 
 
