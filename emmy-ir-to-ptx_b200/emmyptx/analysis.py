@@ -193,6 +193,19 @@ def _tile_axes(tile):
     return [(a.name, dim_value(a.extent)) for a in tile.axes]
 
 
+def _all_f32(stmts):
+    """Every typed statement works on f32 (``Smem`` arrays are typed ``'float'``): the
+    templates load, compute and store f32 only, so any other type is left to a lowering that
+    refuses it by name."""
+    for s in stmts:
+        for attr in ("dtype", "value_dtype"):
+            dt = getattr(s, attr, None)
+            if dt is not None and (dt if isinstance(dt, str) else dtype_name(dt)) \
+                    not in ("f32", "float"):
+                return False
+    return True
+
+
 def lift_pointwise(kernel):
     body = kernel.body
     if len(body) != 1 or type(body[0]).__name__ != "Tile":
@@ -661,7 +674,7 @@ def lift_contraction(kernel):
     allowed = {"Init", "Smem", "CpAsyncCopy", "CpAsyncCommit", "CpAsyncWait", "Loop",
                "StridedLoop", "Sync", "Load", "Assign", "Accum", "Write"}
     stmts = list(walk(tile.body))
-    if any(type(s).__name__ not in allowed for s in stmts):
+    if any(type(s).__name__ not in allowed for s in stmts) or not _all_f32(stmts):
         return None
     if not any(type(s).__name__ == "Accum" for s in stmts):
         return None
@@ -784,7 +797,7 @@ def lift_attention(kernel):
     stmts = list(walk(body[0].body))
     allowed = {"Load", "Assign", "Let", "Init", "Accum", "Loop", "StridedLoop", "Smem",
                "CpAsyncCopy", "CpAsyncCommit", "CpAsyncWait", "Sync", "Write"}
-    if any(type(s).__name__ not in allowed for s in stmts):
+    if any(type(s).__name__ not in allowed for s in stmts) or not _all_f32(stmts):
         return None
     shapes = {a: kernel.shape(a) for a in kernel.arg_order}
     outs = [a["name"] for a in kernel.selected.get("args", ()) if a.get("output")]

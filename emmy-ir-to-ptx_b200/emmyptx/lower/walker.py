@@ -273,7 +273,7 @@ class _Walker:
 
     def s_Assign(self, s):
         if dtype_name(s.dtype) not in (None, "f32"):
-            raise NotImplementedError("only f32 assignments")
+            raise NotImplementedError(f"Assign of {dtype_name(s.dtype)} (only f32 assignments)")
         args = [self._f32(a) for a in s.args]
         if s.name in self.carried and s.name in self.values:
             emit_op(self.gen, op_name(s.op), args, dst=self.values[s.name])

@@ -91,6 +91,9 @@ class PTXKernelGenerator:
                 raise ValueError(f"Duplicate argument metadata: {name}")
             if arg.get("scalar"):
                 raise NotImplementedError(f"scalar (by-value) argument {name!r} is not supported")
+            if arg.get("dtype", "f32") != "f32":     # every buffer is f32 (reference :2297-2306)
+                raise NotImplementedError(f"Unsupported tensor dtype or rank: {name}, "
+                                          f"dtype={arg.get('dtype')}, shape={arg.get('shape')}")
             self.arguments[name] = arg
         if set(self.arguments) != set(self.arg_order):
             raise ValueError("arg_order and args metadata do not match")

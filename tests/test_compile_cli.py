@@ -117,6 +117,32 @@ def test_barrier_ids_and_counts(sync, refused):
             compile_payload(payload, meta, template="walker")
 
 
+_F32_IR = "DataType(name='f32', np=dtype('float32'), nbytes=4)"
+_F16_IR = "DataType(name='f16', np=dtype('float16'), nbytes=2)"
+
+
+@pytest.mark.parametrize("where", ["ir", "meta"])
+@pytest.mark.parametrize("pdir", problem_dirs(), ids=lambda p: p.name)
+def test_other_dtypes_fail_closed(pdir, where):
+    """Every template computes in f32: a fixture retyped to f16, in its IR statements or in
+    meta.json's argument records, is refused (reference compile.py:2297-2306) instead of
+    being compiled as if its buffers held f32."""
+    from emmyptx.emit import compile_payload
+    meta = json.loads((pdir / "meta.json").read_text())
+    for k in meta["kernels"]:
+        payload = json.loads((pdir / f"{k['entry']}.ir.json").read_text())
+        if where == "ir":
+            for node in payload["nodes"].values():
+                if node["op"] == "KernelOp":
+                    node["op_fields"]["body"] = [b.replace(_F32_IR, _F16_IR)
+                                                 for b in node["op_fields"]["body"]]
+        else:
+            k["args"][0]["dtype"] = "f16"
+        one = dict(meta, kernels=[k])
+        with pytest.raises(NotImplementedError, match="f16"):
+            compile_payload(payload, one)
+
+
 LOWERED = problem_dirs()
 
 
