@@ -786,6 +786,122 @@ class AttentionPlan:
     Dv: int
 
 
+_COMMUTATIVE = frozenset({"add", "multiply", "maximum", "minimum"})
+
+
+def _online_softmax_dataflow(body, q, kt, v, scale_buf, smem_src, out) -> bool:
+    """True when the statements compute exactly ``softmax(q @ kt * (1/c)) @ v`` with the online
+    softmax the attention templates implement; the checks above only look at which ops and
+    buffers occur, and a body that arranges the same ops differently (the scale applied
+    after the softmax, another normalisation) must go to a lowering that follows it
+    statement by statement.
+
+    Every value is evaluated symbolically: a load is its global buffer (through the shared
+    array a ``cp.async`` fills), an accumulator read is that accumulator's running value, and
+    add / multiply / maximum arguments are put in a canonical order. Then:
+
+    * each dot accumulator ``D`` adds ``q * kt`` in a seeded loop of its own;
+    * each max accumulator ``M`` takes ``s = D * reciprocal(c)``; with ``g = max(M, s)``,
+      ``alpha = exp(M - g)`` and ``beta = exp(s - g)``, the sum accumulator ``L`` adds ``beta``
+      to ``L * alpha`` and each output accumulator ``O`` adds ``v * beta`` to ``O * alpha``,
+      all in the key loop that encloses ``D``'s loop;
+    * every write, after the key loop, stores ``O * reciprocal(L)`` into the output, and every
+      accumulator is one of these.
+
+    The shapes of the reference's attention IR (``problems/a01_attention``,
+    ``problems/a02_attention_128``) and of the tiled form all have this dataflow."""
+    env, updates, writes = {}, {}, []
+    table = {}                              # expression -> id (equal expressions, equal ids)
+
+    def node(*key):
+        return table.setdefault(key, len(table))
+
+    one = node("lit", 1.0)
+
+    def canon(op, *args):
+        if op == "multiply" and len(args) == 2 and one in args:
+            return args[0] if args[1] == one else args[1]
+        if op in _COMMUTATIVE:
+            args = sorted(args)
+        return node(op, *args)
+
+    def ev(name):
+        return env[name] if name in env else node("acc", name)
+
+    def visit(stmts, path):
+        for st in stmts:
+            kind = type(st).__name__
+            if kind in ("Loop", "StridedLoop"):
+                visit(st.body, path + ((id(st), bool(st.seed)),))
+            elif kind == "Load":
+                src = smem_src.get(st.input, st.input)
+                for nm in st.names:
+                    env[nm] = node("ld", src)
+            elif kind == "Let":
+                val = st.value.value if type(st.value).__name__ == "Literal" else st.value
+                if not isinstance(val, (int, float)):
+                    return False
+                env[st.name] = node("lit", float(val))
+            elif kind == "Assign":
+                env[st.name] = canon(op_name(st.op), *(ev(a) for a in st.args))
+            elif kind == "Accum":
+                if st.name in updates:
+                    return False
+                base = ev(st.base) if st.base is not None else node("acc", st.name)
+                updates[st.name] = (op_name(st.op), base, ev(st.value), path)
+                env[st.name] = node("acc", st.name)
+            elif kind == "Write":
+                if st.output != out:
+                    return False
+                writes.extend((ev(x), path) for x in st.values)
+            elif kind == "Init":
+                return False            # the fixture forms seed their loops instead
+        return True
+
+    if not visit(body, ()):
+        return False
+    dot = canon("multiply", node("ld", q), node("ld", kt))
+    recip = canon("reciprocal", node("ld", scale_buf))
+    D = {n for n, (op, base, val, _) in updates.items()
+         if op == "add" and base == node("acc", n) and val == dot}
+    seen, key_loop, outs = set(D), None, {}
+    for m, (op, base, val, path) in updates.items():
+        if op != "maximum":
+            continue
+        d = next((d for d in D if val == canon("multiply", node("acc", d), recip)), None)
+        if d is None or base != node("acc", m):
+            return False
+        dpath = updates[d][3]
+        if not dpath or not dpath[-1][1] or dpath[:-1] != path:
+            return False                # D's own seeded loop, directly inside the key loop
+        if key_loop not in (None, path):
+            return False
+        key_loop = path
+        s_ = val
+        g = canon("maximum", node("acc", m), s_)
+        alpha = canon("exp", canon("subtract", node("acc", m), g))
+        beta = canon("exp", canon("subtract", s_, g))
+        sums = [n for n, (op2, b2, v2, p2) in updates.items()
+                if op2 == "add" and p2 == path and v2 == beta
+                and b2 == canon("multiply", node("acc", n), alpha)]
+        if len(sums) != 1:
+            return False
+        acc_o = [n for n, (op2, b2, v2, p2) in updates.items()
+                 if op2 == "add" and p2 == path and v2 == canon("multiply", node("ld", v), beta)
+                 and b2 == canon("multiply", node("acc", n), alpha)]
+        for o in acc_o:
+            outs[canon("multiply", node("acc", o), canon("reciprocal", node("acc", sums[0])))] = o
+        seen |= {m, sums[0], *acc_o}
+    if key_loop is None or seen != set(updates) or not outs:
+        return False
+    written = set()
+    for val, path in writes:
+        if val not in outs or len(path) >= len(key_loop) or key_loop[:len(path)] != path:
+            return False
+        written.add(outs[val])
+    return written == set(outs.values())
+
+
 def lift_attention(kernel):
     """Recognise the attention family (reference ``problems/a01_attention``): the body scales
     q.kt dot products by ``reciprocal(c)``, keeps an online (max, sum) softmax with ``exp`` and
@@ -875,6 +991,8 @@ def lift_attention(kernel):
             return None
         cands = picks
     q, kt = cands[0]
+    if not _online_softmax_dataflow(body[0].body, q, kt, vbuf, scale_buf, smem_src, out):
+        return None
     G = 1
     for d in lead:
         G *= d
