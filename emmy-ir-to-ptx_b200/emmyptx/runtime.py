@@ -10,7 +10,6 @@ library or the driver is missing, every call raises :class:`RuntimeError`.
 from __future__ import annotations
 
 import ctypes
-import os
 from pathlib import Path
 
 import numpy as np

@@ -43,7 +43,7 @@ def _check(kind, got, exact, abs_sum=None, label=None):
 @pytest.mark.parametrize("pdir", problem_dirs(), ids=lambda p: p.name)
 def test_fixture_on_gpu(pdir, gpu_runtime):
     from emmyptx.emit import compile_file
-    from oracle.expressions import kernel_inputs, reference_outputs
+    from oracle.expressions import kernel_inputs
     meta = json.loads((pdir / "meta.json").read_text())
     expected = dict(np.load(pdir / "expected.npz"))
     fp64 = None
@@ -59,7 +59,6 @@ def test_fixture_on_gpu(pdir, gpu_runtime):
     if meta["id"][0] in "rf":
         # stricter than the fixture tolerance: within 1e-5 of the exact result
         from oracle.expressions import problem_inputs
-        import oracle.expressions as ex
         args = [a.astype(np.float64) for a in problem_inputs(meta)]
         exact = _exact(meta["id"], args)
         kind = {"f01": "rmsnorm", "f02": "softmax", "f03": "l2norm"}.get(meta["id"][:3], "sum")

@@ -2,7 +2,6 @@
 intermediate stays in device memory, and every fixture folder against its expected.npz."""
 
 import json
-from pathlib import Path
 
 import numpy as np
 import pytest

@@ -1,8 +1,6 @@
 """Multi-kernel problems on CPU: chain validation, per-kernel meta selection, and the chained
 computation evaluated by the oracle's IR interpreter."""
 
-import json
-
 import numpy as np
 import pytest
 

@@ -11,8 +11,6 @@ use. It lives in its own file, collected last, and needs nothing from the other
 tests, so it passes alone in a fresh process as well as after the full suite.
 """
 
-import ctypes
-
 import numpy as np
 import pytest
 
