@@ -115,3 +115,48 @@ def test_pointwise_lift_matches_the_interpreter_under_mutation(tag, payload, met
                                   equal_nan=True), (tag, name, mutated[:200])
         compared += 1
     assert compared >= 1, tag
+
+
+@pytest.mark.parametrize("problem", ["r01_array_sum", "r02_big_sum", "r03_mean", "r04_row_sum",
+                                     "f01_rmsnorm", "f02_row_softmax", "f03_l2norm"])
+def test_row_lift_notices_every_change_of_result(problem, tmp_path):
+    """Reductions and row normalisations: a mutation that changes what the IR computes (the
+    oracle interpreter's output) must change the lifted plan or make the lift decline, so the
+    row template never runs the unmutated program for a body that asks for another."""
+    from emmyptx.analysis import lift_rowreduce
+    from emmyptx.meta import EmmyIRParser
+    from oracle.expressions import kernel_inputs
+    from oracle.ir_eval import run_kernel
+    pdir = PROBLEMS / problem
+    meta = json.loads((pdir / "meta.json").read_text())
+    k = meta["kernels"][0]
+    payload = json.loads((pdir / f"{k['entry']}.ir.json").read_text())
+    node = next(n for n in payload["nodes"].values() if n["op"] == "KernelOp")
+    text = node["op_fields"]["body"][0]
+    inputs = kernel_inputs(k)
+    (tmp_path / "meta.json").write_text(json.dumps(meta))
+
+    def parse(body):
+        node["op_fields"]["body"] = [body]
+        (tmp_path / f"{k['entry']}.ir.json").write_text(json.dumps(payload))
+        return EmmyIRParser(tmp_path / f"{k['entry']}.ir.json", require_meta=True).parse()
+
+    base = parse(text)
+    base_plan = repr(lift_rowreduce(base))
+    assert base_plan != "None"
+    base_out = run_kernel(base, k, inputs)
+    for mutated in _mutations(text, random.Random(problem), 24):
+        try:
+            kernel = parse(mutated)
+        except ValueError:
+            continue
+        if repr(lift_rowreduce(kernel)) != base_plan:
+            continue
+        try:
+            with np.errstate(all="ignore"):
+                out = run_kernel(kernel, k, inputs)
+        except (IndexError, ValueError, NotImplementedError):
+            continue
+        for name, arr in base_out.items():
+            assert np.array_equal(np.asarray(out[name]), np.asarray(arr), equal_nan=True), \
+                (problem, name, mutated[:200])
