@@ -55,6 +55,8 @@ def _read_json(path):
         raise ValueError(f"Cannot read {path}: {exc}") from exc
     except json.JSONDecodeError as exc:
         raise ValueError(f"Invalid JSON in {path}: {exc}") from exc
+    except RecursionError:
+        raise ValueError(f"Invalid JSON in {path}: nested too deeply") from None
     if not isinstance(result, dict):
         raise ValueError(f"Expected a JSON object in {path}")
     return result

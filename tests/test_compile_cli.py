@@ -143,6 +143,14 @@ def test_other_dtypes_fail_closed(pdir, where):
             compile_payload(payload, one)
 
 
+def test_deeply_nested_json_fails_closed(tmp_path):
+    (tmp_path / "k.ir.json").write_text("[" * 200000 + "]" * 200000)
+    (tmp_path / "meta.json").write_text((PROBLEMS / "p00_scalar_add" / "meta.json").read_text())
+    r = run_cli(tmp_path / "k.ir.json")
+    assert r.returncode == 1 and r.stdout == ""
+    assert "nested too deeply" in r.stderr
+
+
 LOWERED = problem_dirs()
 
 
