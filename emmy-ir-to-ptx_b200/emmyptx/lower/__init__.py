@@ -65,6 +65,27 @@ _EMITTERS = {"matmul": "lower_contraction", "attention": "lower_attention",
              "reduce": "lower_rowreduce", "pointwise": "lower_pointwise"}
 
 
+def _check_launch(launch) -> None:
+    """The meta.json launch record must describe a launch CUDA can make: grid and block of
+    three positive integers, at most 1024 threads per CTA (z at most 64), grid y and z at most
+    65535, and a non-negative integer ``smem_bytes``. The templates size their work from these
+    numbers, so a record outside them is refused instead of compiled into a kernel that could
+    not be launched as described."""
+    for field in ("grid", "block"):
+        v = launch.get(field, [1, 1, 1])
+        if not (isinstance(v, (list, tuple)) and len(v) == 3
+                and all(type(x) is int and x >= 1 for x in v)):
+            raise ValueError(f"launch {field} must be three positive integers, got {v!r}")
+    block, grid = launch.get("block", [1, 1, 1]), launch.get("grid", [1, 1, 1])
+    if block[0] * block[1] * block[2] > 1024 or block[2] > 64:
+        raise ValueError(f"launch block {list(block)} exceeds 1024 threads per CTA")
+    if grid[0] > 2**31 - 1 or grid[1] > 65535 or grid[2] > 65535:
+        raise ValueError(f"launch grid {list(grid)} exceeds the grid limits")
+    smem = launch.get("smem_bytes", 0) or 0
+    if type(smem) is not int or smem < 0:
+        raise ValueError(f"launch smem_bytes must be a non-negative integer, got {smem!r}")
+
+
 class EmmyIRLowering:
     """Lower one parsed kernel to the text of its ``.entry`` (module declarations first)."""
 
@@ -109,6 +130,7 @@ class EmmyIRLowering:
         yield "pointwise", (lambda: lift_pointwise(k)), "pointwise"
 
     def lower(self) -> str:
+        _check_launch(self.kernel.launch)
         for name, lift, emit in self._candidates():
             if self.force and self.force not in (name, "auto"):
                 continue

@@ -143,6 +143,23 @@ def test_other_dtypes_fail_closed(pdir, where):
             compile_payload(payload, one)
 
 
+@pytest.mark.parametrize("field,value", [("block", [0, 1, 1]), ("block", [2048, 1, 1]),
+                                         ("block", ["128", 1, 1]), ("grid", [0, 1, 1]),
+                                         ("grid", [-4, 1, 1]), ("grid", [1, 70000, 1]),
+                                         ("block", [128, 1]), ("smem_bytes", -1)])
+def test_impossible_launch_records_fail_closed(field, value):
+    """A meta.json launch CUDA could not make is refused before any template sizes its work
+    from it."""
+    from emmyptx.emit import compile_payload
+    for problem in ("p01_vector_add", "m01_matmul_512"):
+        pdir = PROBLEMS / problem
+        meta = json.loads((pdir / "meta.json").read_text())
+        meta["kernels"][0][field] = value
+        payload = json.loads(next(pdir.glob("*.ir.json")).read_text())
+        with pytest.raises(ValueError, match=f"launch {field}"):
+            compile_payload(payload, meta)
+
+
 def test_deeply_nested_json_fails_closed(tmp_path):
     (tmp_path / "k.ir.json").write_text("[" * 200000 + "]" * 200000)
     (tmp_path / "meta.json").write_text((PROBLEMS / "p00_scalar_add" / "meta.json").read_text())
