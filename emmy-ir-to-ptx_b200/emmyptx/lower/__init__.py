@@ -71,10 +71,13 @@ def _check_launch(launch) -> None:
     65535, and a non-negative integer ``smem_bytes``. The templates size their work from these
     numbers, so a record outside them is refused instead of compiled into a kernel that could
     not be launched as described."""
+    def count(x):                       # an integer of any integral type, not a bool
+        return hasattr(x, "__index__") and not isinstance(x, bool)
+
     for field in ("grid", "block"):
         v = launch.get(field, [1, 1, 1])
         if not (isinstance(v, (list, tuple)) and len(v) == 3
-                and all(type(x) is int and x >= 1 for x in v)):
+                and all(count(x) and x >= 1 for x in v)):
             raise ValueError(f"launch {field} must be three positive integers, got {v!r}")
     block, grid = launch.get("block", [1, 1, 1]), launch.get("grid", [1, 1, 1])
     if block[0] * block[1] * block[2] > 1024 or block[2] > 64:
@@ -82,7 +85,7 @@ def _check_launch(launch) -> None:
     if grid[0] > 2**31 - 1 or grid[1] > 65535 or grid[2] > 65535:
         raise ValueError(f"launch grid {list(grid)} exceeds the grid limits")
     smem = launch.get("smem_bytes", 0) or 0
-    if type(smem) is not int or smem < 0:
+    if not count(smem) or smem < 0:
         raise ValueError(f"launch smem_bytes must be a non-negative integer, got {smem!r}")
 
 
